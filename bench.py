@@ -1,0 +1,397 @@
+#!/usr/bin/env python
+"""Benchmark of the fused FP8 quant + GEMV decode path on B200.
+
+Workload (one "step" = one decode step's linear stack at M = 1): the Qwen3-8B
+FP8 decoder's four block-FP8 linears -- qkv 4096->6144, o 4096->4096,
+gate_up 4096->24576, down 12288->4096 -- for each of 36 layers, every layer
+with its own seeded random e4m3 weights and 128x128 fp32 block scales
+(W ~ N(0, 0.02^2) block-quantised, activations bf16 ~ N(0, 1) with 1% of the
+channels x20).  6.95 GB of weights per step, far larger than the 126 MB L2,
+so no L2 flush is needed between steps.  With --gpus N > 1 every linear is
+sharded by output rows across the ranks and its bf16 output is all-gathered
+(NCCL) after it, so the total work is fixed (strong scaling).
+
+value     algorithmic bytes per step / device time per step (CUDA graph of one
+          step, CUDA events, max over ranks), in GB/s (whole job).
+e2e       the same metric through the public API (fp8gq.fused_gemv_quant,
+          eager) with the step's activations copied in from pinned host
+          memory and the outputs copied back, inside the timed region.
+roofline  the dominant kernel (gate_up, row kernel): algorithmic bytes per
+          launch / average launch duration (CUDA graph of 36 launches on
+          distinct weights), against MEASURED_PEAKS.json's hbm_gbs.
+cpu_baseline  the reference's PyTorch path (quantise, dequantise, fp32 matmul)
+          on the host cores, on a bounded sample (rank 0, N = 1 only).
+
+--impl reference runs that CPU reference path alone (rank 0; the other ranks
+exit), one linear of the stack per step in rotation.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO, REPO / "sglang-triton-fusion_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+LAYERS = 36
+SHAPES = [("qkv", 4096, 6144), ("o", 4096, 4096), ("gate_up", 4096, 24576), ("down", 12288, 4096)]
+METRIC = "fused FP8 quant+GEMV achieved HBM GB/s, M=1, Qwen3-8B decode linear stack (36 layers)"
+WORKLOAD = ("qwen3-8b-fp8 decode linear stack, M=1: 36 layers x {qkv 4096->6144, o 4096->4096, "
+            "gate_up 4096->24576, down 12288->4096}, e4m3 weights with 128x128 fp32 block scales, "
+            "bf16 activations with 1x128 group quant")
+
+
+def alg_bytes(M: int, K: int, N: int) -> int:
+    """N*K weight bytes + fp32 block scales + bf16 activation in + bf16 out."""
+    return N * K + 4 * (N // 128) * (K // 128) + 2 * M * K + 2 * M * N
+
+
+STEP_BYTES = LAYERS * sum(alg_bytes(1, K, N) for _, K, N in SHAPES)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--e2e-steps", type=int, default=100)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------- clocks --
+class ClockSampler:
+    """nvidia-smi samples of the GPU this rank runs on, during the timed region."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None):
+        self.uuid = uuid
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            if self.uuid and self.uuid not in f[0]:
+                continue
+            try:
+                rows.append((float(f[1]), float(f[2]), f[4], f[5], f[6], f[7], f[8]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[3:]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# ---------------------------------------------------------- CPU path --
+def cpu_reference_sample(seconds: float = 12.0, linears: int | None = None):
+    """The reference's PyTorch path on the host cores over one layer's four
+    linears (round robin) until `seconds` pass; returns (GB/s, cores, sample)."""
+    import torch
+    from oracle import fp8gq_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    ops = []
+    for i, (name, K, N) in enumerate(SHAPES):
+        x = torch.from_numpy(O.make_activation(1, K, seed=1000 + i)).bfloat16()
+        wq, ws = O.make_weight(N, K, seed=2000 + i)
+        ops.append((name, K, N, x, torch.from_numpy(wq).view(torch.float8_e4m3fn), torch.from_numpy(ws)))
+    O.torch_reference_path(ops[0][3], ops[0][4], ops[0][5])        # warm
+    done_bytes, t_total, n = 0, 0.0, 0
+    while (linears is None and t_total < seconds) or (linears is not None and n < linears):
+        name, K, N, x, w, s = ops[n % len(ops)]
+        t0 = time.perf_counter()
+        O.torch_reference_path(x, w, s)
+        t_total += time.perf_counter() - t0
+        done_bytes += alg_bytes(1, K, N)
+        n += 1
+    return done_bytes / t_total / 1e9, torch.get_num_threads(), \
+        f"{n} linears of one Qwen3-8B layer (qkv, o, gate_up, down round robin), M=1, full path incl. weight dequant"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+    from oracle import fp8gq_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    ops = []
+    for i, (name, K, N) in enumerate(SHAPES):
+        x = torch.from_numpy(O.make_activation(1, K, seed=1000 + i)).bfloat16()
+        wq, ws = O.make_weight(N, K, seed=2000 + i)
+        ops.append((K, N, x, torch.from_numpy(wq).view(torch.float8_e4m3fn), torch.from_numpy(ws)))
+    for j in range(args.warmup):
+        K, N, x, w, s = ops[j % 4]
+        O.torch_reference_path(x, w, s)
+    t = 0.0
+    total = 0
+    for j in range(args.steps):
+        K, N, x, w, s = ops[j % 4]
+        t0 = time.perf_counter()
+        O.torch_reference_path(x, w, s)
+        t += time.perf_counter() - t0
+        total += alg_bytes(1, K, N)
+    gbs = total / t / 1e9
+    cores = torch.get_num_threads()
+    sample = ("one linear of a Qwen3-8B layer per step (qkv, o, gate_up, down round robin), M=1, "
+              "torch CPU: group quant, dequant, fp32 matmul, bf16 out")
+    line = {"metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t / args.steps * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out",
+            "data": "synthetic (seeded)",
+            "config": {"workload": WORKLOAD, "sample": sample, "M": 1},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------- GPU path --
+def make_weight_gpu(N, K, seed, dev):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = (torch.randn(N, K, generator=g, device=dev) * 0.02).bfloat16().float()
+    blk = w.view(N // 128, 128, K // 128, 128)
+    ws = blk.abs().amax(dim=(1, 3)).clamp_min(1e-10) / 448.0
+    q = (blk / ws[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(N, K)
+    return q.contiguous(), ws.contiguous()
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import fp8gq
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    fp8gq.load()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- operands: each rank owns rows [r*N/world, (r+1)*N/world) of every linear
+    layers = []
+    xs_len = sum(K for _, K, _ in SHAPES)
+    out_len = sum(N for _, _, N in SHAPES)
+    x_all = torch.empty(LAYERS, xs_len, dtype=torch.bfloat16, device=dev)
+    out_all = torch.empty(LAYERS, out_len, dtype=torch.bfloat16, device=dev)
+    shard_all = torch.empty(LAYERS, out_len // world, dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for L in range(LAYERS):
+        lin = []
+        xo = oo = so = 0
+        for i, (name, K, N) in enumerate(SHAPES):
+            Nr = N // world
+            wq, ws = make_weight_gpu(Nr, K, seed=100000 * L + 1000 * i + rank, dev=dev)
+            x = x_all[L, xo:xo + K].view(1, K)
+            xv = torch.randn(1, K, generator=g, device=dev)
+            ch = torch.randperm(K, generator=g, device=dev)[: round(0.01 * K)]
+            xv[:, ch] *= 20.0
+            x.copy_(xv.bfloat16())
+            lin.append((name, K, N, wq, ws, x, out_all[L, oo:oo + N].view(1, N),
+                        shard_all[L, so:so + Nr].view(1, Nr)))
+            xo += K
+            oo += N
+            so += Nr
+        layers.append(lin)
+    torch.cuda.synchronize()
+
+    def step():
+        for lin in layers:
+            for name, K, N, wq, ws, x, out, shard in lin:
+                if world == 1:
+                    fp8gq.fused_gemv_quant(x, wq, ws, out=out)
+                else:
+                    fp8gq.fused_gemv_quant(x, wq, ws, out=shard)
+                    dist.all_gather_into_tensor(out.view(-1), shard.view(-1))
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    barrier()
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+
+    # ---- timed region: K steps (graph replays), CUDA events, max over ranks
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(uuid)
+    with sampler:
+        time.sleep(0.3)
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(end) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = sampler.summary()
+    value = STEP_BYTES / (ms * 1e-3) / 1e9
+    launches = LAYERS * len(SHAPES) * args.steps
+
+    # ---- per-linear device time: graph of the 36 launches of one shape
+    per = {}
+    for i, (name, K, N) in enumerate(SHAPES):
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            for lin in layers:
+                _, _, _, wq, ws, x, out, shard = lin[i]
+                fp8gq.fused_gemv_quant(x, wq, ws, out=out if world == 1 else shard)
+        g1.replay()
+        torch.cuda.synchronize()
+        reps = 20
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            g1.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) * 1e3 / (reps * LAYERS)
+        b = alg_bytes(1, K, N // world)
+        per[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                     "bytes_per_call": b}
+        del g1
+    peak, peak_kind = measured_peak()
+    gu = per["gate_up"]
+    roofline = {"bound": "hbm", "achieved": gu["gbs"], "peak": peak, "unit": "GB/s",
+                "frac": round(gu["gbs"] / peak, 4), "traffic": None,
+                "kernel": "gemv_row_kernel<1,4,false> (gate_up 4096->24576%s)" % (
+                    f", N/{world} rows per rank" if world > 1 else ""),
+                "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)"}
+
+    # ---- e2e: public API, eager, host buffers in and out
+    x_host = torch.empty_like(x_all, device="cpu").pin_memory()
+    x_host.copy_(x_all.cpu())
+    o_host = torch.empty_like(out_all, device="cpu").pin_memory()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for it in range(3 + args.e2e_steps):
+        if it == 3:
+            barrier()
+            torch.cuda.synchronize()
+            e0.record()
+        x_all.copy_(x_host, non_blocking=True)
+        step()
+        o_host.copy_(out_all, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+           "h2d_bytes_per_step": x_all.numel() * 2, "d2h_bytes_per_step": out_all.numel() * 2,
+           "ms_per_step": round(e2e_ms, 4), "path": "fp8gq.fused_gemv_quant (eager) per linear"}
+
+    torch.cuda.synchronize()
+    assert fp8gq.device_error() == 0, "a kernel recorded a wait timeout"
+    del graph
+    barrier()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, cores, sample = cpu_reference_sample()
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "e4m3 x e4m3 -> fp32 accumulate, bf16 out", "data": "synthetic (seeded)",
+                "config": {"workload": WORKLOAD, "M": 1, "layers": LAYERS,
+                           "bytes_per_step": STEP_BYTES,
+                           "l2": "inputs larger than L2 (6.95 GB of weights per step, 126 MB L2)",
+                           "parallelism": f"N-sharded x{world} + NCCL all-gather per linear" if world > 1
+                           else "single GPU", "timing": "CUDA graph of one step, CUDA events"},
+                "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
+                "per_linear": per, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "gpu_launches": launches, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,129 @@
+/*
+ * fp8gq -- fused FP8 (e4m3) activation group-quant + block-scaled GEMV for
+ * NVIDIA B200 (sm_100a).  C ABI: plain pointers, sizes and strides; no torch
+ * or CUDA types in the signatures.  Every entry point is asynchronous on the
+ * given stream, allocates nothing, and returns FP8GQ_OK or an error status
+ * (it never aborts the process).
+ *
+ * Operand conventions, identical to the reference's
+ * (wafik/sglang-triton-fusion, kernels/fused_gemv_quant_tm.py:83-102):
+ *   x    bf16  [M, K]    row stride ldx elements (>= K)
+ *   w    e4m3  [N, K]    row stride ldw bytes (>= K), one byte per weight
+ *   ws   fp32  [N/128, K/128]  row stride ldws elements (sglang's
+ *                              weight_scale_inv, one scale per 128x128 block)
+ *   out  bf16  [M, N]    row stride ldo elements (>= N)
+ *   K % 128 == 0 and N % 128 == 0 (kernels/fused_gemv_quant_tm.py:87).
+ * The activation is quantised per row and per 128-column group:
+ *   amax = max(max|x|, 1e-10); sx = amax / 448; xq = e4m3_rne(clamp(x / sx))
+ * (x * (1/sx) exactly as sglang fp8_kernel.py:170-173 writes it) and
+ *   out[m, n] = bf16( sum_b (sum_{k in b} xq[m,k] w[n,k]) * sx[m,b] * ws[n/128,b] ).
+ *
+ * Optional outputs xq_out (uint8 [M, K], row stride K) and sx_out (fp32
+ * [M, K/128], row stride K/128) receive the quantised activation bytes and
+ * scales the fused kernel computed internally; pass NULL to skip them.
+ *
+ * `stream` is a cudaStream_t (NULL = the legacy default stream).
+ */
+#ifndef FP8GQ_H_
+#define FP8GQ_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FP8GQ_VERSION 1
+
+enum fp8gq_status {
+    FP8GQ_OK = 0,
+    FP8GQ_ERR_NULL_POINTER = 1,  /* a required pointer is NULL                      */
+    FP8GQ_ERR_SHAPE = 2,         /* M < 1, or K / N not a positive multiple of 128  */
+    FP8GQ_ERR_ALIGNMENT = 3,     /* x / w / gu not 16-byte aligned, or a stride not
+                                    a multiple of 16 bytes                          */
+    FP8GQ_ERR_STRIDE = 4,        /* a row stride smaller than the row length        */
+    FP8GQ_ERR_WORKSPACE = 5,     /* workspace NULL or smaller than required         */
+    FP8GQ_ERR_DEVICE = 6,        /* current device is not compute capability 10.x   */
+    FP8GQ_ERR_LAUNCH = 7,        /* the CUDA launch failed                          */
+    FP8GQ_ERR_UNSUPPORTED = 8,   /* shape outside what the selected kernel handles  */
+    FP8GQ_ERR_DEVICE_TIMEOUT = 9 /* a kernel's bounded wait gave up (see
+                                    fp8gq_device_error)                             */
+};
+
+typedef void *fp8gq_stream_t;
+
+/* Library version (FP8GQ_VERSION). */
+int fp8gq_version(void);
+
+/* Static, human-readable text for a status code. */
+const char *fp8gq_status_string(int status);
+
+/* Fused quant + GEMV, routed by M exactly like the reference wrapper
+ * fused_gemv_quant (kernels/fused_gemv_quant_tm.py:83-102): M == 1 runs the
+ * row kernel (fp8gq_gemv_quant_row), M > 1 the tensor-core tile kernel
+ * (fp8gq_gemv_quant_tm).  `workspace` must hold fp8gq_workspace_bytes(M, N, K)
+ * bytes (it may be NULL when that is 0) and be zero-filled before its first
+ * use; kernels leave it zero-filled again when they finish.  Calls that share
+ * a workspace must not overlap on the GPU. */
+int fp8gq_fused_gemv_quant(const void *x, int64_t ldx, const void *w, int64_t ldw,
+                           const float *ws, int64_t ldws, void *out, int64_t ldo,
+                           int M, int N, int K, uint8_t *xq_out, float *sx_out,
+                           void *workspace, size_t workspace_bytes, fp8gq_stream_t stream);
+
+/* Scratch bytes fp8gq_fused_gemv_quant / fp8gq_fused_swiglu_q_gemm need for
+ * this shape (0 when the routed kernel needs none).  K is the contraction
+ * length (I for the SwiGLU entry point). */
+size_t fp8gq_workspace_bytes(int M, int N, int K);
+
+/* M == 1 row kernel: one pass over the weight on CUDA cores, 128-bit bulk
+ * copies into a shared-memory ring, warp-shuffle amax, fp32 accumulation.
+ * Replaces gemv_quant_row_kernel (kernels/fused_gemv_quant_tm.py:25-46) and
+ * its twin gemv_quant_kernel (kernels/fused_gemv_quant.py:21-46).
+ * Requires M == 1 and K <= 49152. */
+int fp8gq_gemv_quant_row(const void *x, const void *w, int64_t ldw,
+                         const float *ws, int64_t ldws, void *out,
+                         int N, int K, uint8_t *xq_out, float *sx_out,
+                         fp8gq_stream_t stream);
+
+/* Tile kernel for any M >= 1 (tcgen05 FP8 MMA, each weight tile read once
+ * for all M rows, M <= 256 per pass).  Replaces gemv_quant_tm_kernel
+ * (kernels/fused_gemv_quant_tm.py:49-80). */
+int fp8gq_gemv_quant_tm(const void *x, int64_t ldx, const void *w, int64_t ldw,
+                        const float *ws, int64_t ldws, void *out, int64_t ldo,
+                        int M, int N, int K, uint8_t *xq_out, float *sx_out,
+                        void *workspace, size_t workspace_bytes, fp8gq_stream_t stream);
+
+/* Fused SwiGLU + quant + GEMV (down_proj):
+ *   act = silu(gu[:, :I]) * gu[:, I:]   (fp32),   out = GEMV(quant(act), w)
+ * gu bf16 [M, 2I] row stride ldgu, w e4m3 [N, I], ws [N/128, I/128].
+ * Replaces fused_swiglu_q_gemm / swiglu_q_gemm_kernel
+ * (kernels/fused_swiglu_quant_gemv.py:26-67).  xq_out / sx_out as above,
+ * with K = I. */
+int fp8gq_fused_swiglu_q_gemm(const void *gu, int64_t ldgu, const void *w, int64_t ldw,
+                              const float *ws, int64_t ldws, void *out, int64_t ldo,
+                              int M, int N, int I, uint8_t *xq_out, float *sx_out,
+                              void *workspace, size_t workspace_bytes, fp8gq_stream_t stream);
+
+/* Activation group quant alone (the same device code the fused kernels
+ * run): x bf16 [M, K] -> xq uint8 [M, K] (row stride K), sx fp32 [M, K/128].
+ * Mirrors sglang's per-token-group quant as inlined at
+ * kernels/fused_gemv_quant.py:35-43. */
+int fp8gq_group_quant(const void *x, int64_t ldx, int M, int K,
+                      uint8_t *xq, float *sx, fp8gq_stream_t stream);
+
+/* SwiGLU + group quant alone: gu bf16 [M, 2I] -> xq [M, I], sx [M, I/128]
+ * (kernels/fused_swiglu_quant_gemv.py:40-46). */
+int fp8gq_swiglu_group_quant(const void *gu, int64_t ldgu, int M, int I,
+                             uint8_t *xq, float *sx, fp8gq_stream_t stream);
+
+/* Reads (and with clear != 0 resets) the current device's error word, which
+ * a kernel sets when one of its bounded waits gives up.  Synchronous.  0 means
+ * no error was recorded. */
+int fp8gq_device_error(uint32_t *code, int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP8GQ_H_ */

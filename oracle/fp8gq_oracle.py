@@ -235,15 +235,18 @@ def gemv_from_quant(xq: np.ndarray, sx: np.ndarray, wq: np.ndarray, ws: np.ndarr
     with the per-block factor formed in fp32 as the reference does
     (kernels/fused_gemv_quant_tm.py:45)."""
     xv = E4M3_TABLE[np.asarray(xq, dtype=np.uint8)].astype(np.float64)
-    wv = E4M3_TABLE[np.asarray(wq, dtype=np.uint8)].astype(np.float64)
+    wv = E4M3_TABLE[np.asarray(wq, dtype=np.uint8)]
     M, K = xv.shape
     N = wv.shape[0]
-    nb, kb = N // GROUP, K // GROUP
-    # per-block partials: [M, kb, N]
-    part = np.einsum("mbk,nbk->mbn", xv.reshape(M, kb, GROUP), wv.reshape(N, kb, GROUP))
-    scale = (np.asarray(sx, np.float32)[:, :, None]
-             * np.repeat(np.asarray(ws, np.float32).T, GROUP, axis=1)[None, :, :]).astype(np.float32)
-    return (part * scale.astype(np.float64)).sum(axis=1)
+    sx = np.asarray(sx, np.float32)
+    ws = np.asarray(ws, np.float32)
+    out = np.zeros((M, N), np.float64)
+    for b in range(K // GROUP):
+        cols = slice(b * GROUP, (b + 1) * GROUP)
+        part = xv[:, cols] @ wv[:, cols].astype(np.float64).T          # exact: <= 2^-18 granularity
+        scale = (sx[:, b][:, None] * np.repeat(ws[:, b], GROUP)[None, :]).astype(np.float32)
+        out += part * scale.astype(np.float64)
+    return out
 
 
 def fused_gemv_quant(x: np.ndarray, wq: np.ndarray, ws: np.ndarray):
@@ -296,32 +299,39 @@ def north_star_ok(got: np.ndarray, ref: np.ndarray, rtol: float = 1e-2, atol_rel
 def make_activation(M: int, K: int, seed: int, std: float = 1.0, outlier_frac: float = 0.01,
                     outlier_scale: float = 20.0) -> np.ndarray:
     """bf16 ~N(0, std^2) with `outlier_frac` of the channels scaled by
-    `outlier_scale` (channels picked by a seeded permutation)."""
-    rng = np.random.default_rng(seed)
-    x = rng.standard_normal((M, K)).astype(np.float32) * _F32(std)
+    `outlier_scale` (channels picked by a seeded permutation).  Seeded torch
+    CPU generator; returns float32 holding bf16 values."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    x = torch.randn(M, K, generator=g) * float(std)
     n_out = int(round(outlier_frac * K))
     if n_out:
-        ch = rng.permutation(K)[:n_out]
-        x[:, ch] *= _F32(outlier_scale)
-    return bf16_round(x)
+        ch = torch.randperm(K, generator=g)[:n_out]
+        x[:, ch] *= float(outlier_scale)
+    return x.to(torch.bfloat16).float().numpy()
 
 
 def quantize_weight_blocks(w: np.ndarray):
     """bf16/fp32 W [N, K] -> (Wq uint8, Ws float32 [N/128, K/128]) with
-    ws = max(amax_block, eps) / 448 and Wq = e4m3(clamp(W / ws, +-448))."""
-    w = np.asarray(w, dtype=np.float32)
-    N, K = w.shape
-    blk = w.reshape(N // GROUP, GROUP, K // GROUP, GROUP)
-    amax = np.maximum(np.abs(blk).max(axis=(1, 3)), EPS)
-    ws = (amax / E4M3_MAX).astype(np.float32)
-    q = np.clip((blk / ws[:, None, :, None]).astype(np.float32), -E4M3_MAX, E4M3_MAX)
-    return e4m3_encode_rne(q).reshape(N, K), ws
+    ws = max(amax_block, eps) / 448 and Wq = e4m3_rne(clamp(W / ws, +-448)),
+    every step an fp32 operation (torch on CPU; its e4m3 cast is the RNE cast
+    e4m3_encode_rne implements, which the tests check)."""
+    import torch
+    t = torch.as_tensor(np.asarray(w, np.float32))
+    N, K = t.shape
+    blk = t.view(N // GROUP, GROUP, K // GROUP, GROUP)
+    amax = blk.abs().amax(dim=(1, 3)).clamp_min(float(EPS))
+    ws = amax / float(E4M3_MAX)
+    q = (blk / ws[:, None, :, None]).clamp(-float(E4M3_MAX), float(E4M3_MAX)).to(torch.float8_e4m3fn)
+    return q.view(torch.uint8).reshape(N, K).numpy(), ws.numpy().astype(np.float32)
 
 
 def make_weight(N: int, K: int, seed: int, std: float = 0.02):
-    rng = np.random.default_rng(seed)
-    w = bf16_round(rng.standard_normal((N, K)).astype(np.float32) * _F32(std))
-    return quantize_weight_blocks(w)
+    """Weight ~N(0, std^2) in bf16, block-quantised to e4m3 (seeded)."""
+    import torch
+    g = torch.Generator().manual_seed(int(seed))
+    w = (torch.randn(N, K, generator=g) * float(std)).to(torch.bfloat16).float()
+    return quantize_weight_blocks(w.numpy())
 
 
 # --------------------------------------------------------------------------

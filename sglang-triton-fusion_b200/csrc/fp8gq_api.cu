@@ -1,0 +1,274 @@
+// C ABI of libfp8gq (declared in include/fp8gq.h): argument checks, kernel
+// selection and launch.  No allocation happens here; the tile kernel's scratch
+// is the caller's workspace.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "../../include/fp8gq.h"
+#include "fp8gq_device.cuh"
+#include "gemm_tm.cuh"
+#include "gemv_row.cuh"
+#include "quant_only.cuh"
+
+using namespace fp8gq;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  int sm_count = 0;
+  int cc_major = 0;
+  int max_smem_optin = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+
+int device_info(DeviceInfo* out, int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FP8GQ_ERR_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sm_count == 0) {
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+            cudaSuccess) {
+      d.sm_count = 0;
+      return FP8GQ_ERR_DEVICE;
+    }
+  }
+  if (d.cc_major != 10) return FP8GQ_ERR_DEVICE;
+  *out = d;
+  if (dev_out) *dev_out = dev;
+  return FP8GQ_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(const void* x, const void* w, const float* ws, const void* out, int M, int N, int K,
+                 int64_t ldw, int64_t ldws, int64_t ldo) {
+  if (!x || !w || !ws || !out) return FP8GQ_ERR_NULL_POINTER;
+  if (M < 1 || N <= 0 || K <= 0 || (N % kGroup) != 0 || (K % kGroup) != 0) return FP8GQ_ERR_SHAPE;
+  if (ldw < K || ldws < K / kGroup || ldo < N) return FP8GQ_ERR_STRIDE;
+  if (!aligned16(x) || !aligned16(w) || (ldw % 16) != 0) return FP8GQ_ERR_ALIGNMENT;
+  if ((reinterpret_cast<uintptr_t>(ws) & 3u) != 0 || (reinterpret_cast<uintptr_t>(out) & 1u) != 0)
+    return FP8GQ_ERR_ALIGNMENT;
+  return FP8GQ_OK;
+}
+
+inline int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? FP8GQ_OK : FP8GQ_ERR_LAUNCH;
+}
+
+// ----------------------------------------------------------------- row --
+using RowKernel = void (*)(const RowParams);
+
+template <int C, int R, bool S>
+RowKernel row_fn() {
+  return gemv_row_kernel<C, R, S>;
+}
+
+constexpr int kRowCs[] = {1, 2, 3, 4, 6, 8};
+constexpr int kRowRs[] = {1, 2, 4};
+
+template <bool S>
+RowKernel row_lookup(int ci, int ri) {
+  static const RowKernel table[6][3] = {
+      {row_fn<1, 1, S>(), row_fn<1, 2, S>(), row_fn<1, 4, S>()},
+      {row_fn<2, 1, S>(), row_fn<2, 2, S>(), row_fn<2, 4, S>()},
+      {row_fn<3, 1, S>(), row_fn<3, 2, S>(), row_fn<3, 4, S>()},
+      {row_fn<4, 1, S>(), row_fn<4, 2, S>(), row_fn<4, 4, S>()},
+      {row_fn<6, 1, S>(), row_fn<6, 2, S>(), row_fn<6, 4, S>()},
+      {row_fn<8, 1, S>(), row_fn<8, 2, S>(), row_fn<8, 4, S>()},
+  };
+  return table[ci][ri];
+}
+
+constexpr int kRowMaxK = 8 * 384 * 16;      // C = 8 chunks of 16 per thread, T <= 384
+constexpr int kRowRingBytes = 96 * 1024;    // per CTA; two CTAs per SM
+
+int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const float* ws, int64_t ldws,
+               void* out, int N, int K, uint8_t* xq_out, float* sx_out, cudaStream_t stream) {
+  DeviceInfo di;
+  int dev = 0;
+  int st = device_info(&di, &dev);
+  if (st != FP8GQ_OK) return st;
+  if (K > kRowMaxK) return FP8GQ_ERR_UNSUPPORTED;
+  const int n_chunks = K / 16;
+  const int c_need = (n_chunks + 383) / 384;
+  int ci = 0;
+  while (kRowCs[ci] < c_need) ++ci;
+  const int C = kRowCs[ci];
+  const int T = ((n_chunks + C - 1) / C + 31) / 32 * 32;
+  int ri = 2;
+  while (ri > 0 && kRowRs[ri] * K > 16384) --ri;
+  const int R = kRowRs[ri];
+  const int stage_bytes = R * K;
+  int stages = kRowRingBytes / stage_bytes;
+  if (stages > 16) stages = 16;
+  if (stages < 2) stages = 2;
+  const size_t smem = row_smem_bytes(stages, stage_bytes, T / 32);
+  if (smem > static_cast<size_t>(di.max_smem_optin)) return FP8GQ_ERR_UNSUPPORTED;
+
+  RowKernel fn = swiglu ? row_lookup<true>(ci, ri) : row_lookup<false>(ci, ri);
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+      cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+
+  RowParams p;
+  p.x = static_cast<const __nv_bfloat16*>(x);
+  p.w = static_cast<const uint8_t*>(w);
+  p.ldw = ldw;
+  p.ws = ws;
+  p.ldws = ldws;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.N = N;
+  p.K = K;
+  p.n_groups = N / R;
+  p.stages = stages;
+  p.xq_out = xq_out;
+  p.sx_out = sx_out;
+  int grid = 2 * di.sm_count;
+  if (grid > p.n_groups) grid = p.n_groups;
+  fn<<<grid, T + 32, smem, stream>>>(p);
+  return launch_status();
+}
+
+int launch_quant(bool swiglu, const void* x, int64_t ldx, int M, int K, uint8_t* xq, float* sx,
+                 cudaStream_t stream) {
+  DeviceInfo di;
+  int st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  const int64_t groups = static_cast<int64_t>(M) * (K / kGroup);
+  const int64_t blocks = (groups + 7) / 8;
+  if (blocks > 0x7fffffff) return FP8GQ_ERR_UNSUPPORTED;
+  if (swiglu)
+    group_quant_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, M, K, xq, sx);
+  else
+    group_quant_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, M, K, xq, sx);
+  return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+int fp8gq_version(void) { return FP8GQ_VERSION; }
+
+const char* fp8gq_status_string(int status) {
+  switch (status) {
+    case FP8GQ_OK: return "ok";
+    case FP8GQ_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case FP8GQ_ERR_SHAPE: return "bad shape: need M >= 1 and K, N positive multiples of 128";
+    case FP8GQ_ERR_ALIGNMENT: return "misaligned operand: x, w and gu need 16-byte alignment and 16-byte row strides";
+    case FP8GQ_ERR_STRIDE: return "a row stride is smaller than its row";
+    case FP8GQ_ERR_WORKSPACE: return "workspace missing or too small (see fp8gq_workspace_bytes)";
+    case FP8GQ_ERR_DEVICE: return "current CUDA device is not compute capability 10.x (B200, sm_100a)";
+    case FP8GQ_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case FP8GQ_ERR_UNSUPPORTED: return "shape not supported by the selected kernel";
+    case FP8GQ_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait gave up (fp8gq_device_error has the site)";
+    default: return "unknown fp8gq status";
+  }
+}
+
+int fp8gq_gemv_quant_row(const void* x, const void* w, int64_t ldw, const float* ws, int64_t ldws,
+                         void* out, int N, int K, uint8_t* xq_out, float* sx_out,
+                         fp8gq_stream_t stream) {
+  int st = check_common(x, w, ws, out, 1, N, K, ldw, ldws, N);
+  if (st != FP8GQ_OK) return st;
+  return launch_row(false, x, w, ldw, ws, ldws, out, N, K, xq_out, sx_out,
+                    static_cast<cudaStream_t>(stream));
+}
+
+size_t fp8gq_workspace_bytes(int M, int N, int K) {
+  if (M < 1 || N <= 0 || K <= 0 || N % kGroup || K % kGroup) return 0;
+  if (M == 1 && K <= kRowMaxK) return 0;
+  return tm_workspace_bytes(M, N, K);
+}
+
+int fp8gq_gemv_quant_tm(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
+                        int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
+                        float* sx_out, void* workspace, size_t workspace_bytes,
+                        fp8gq_stream_t stream) {
+  int st = check_common(x, w, ws, out, M, N, K, ldw, ldws, ldo);
+  if (st != FP8GQ_OK) return st;
+  if (ldx < K || (ldx % 8) != 0) return ldx < K ? FP8GQ_ERR_STRIDE : FP8GQ_ERR_ALIGNMENT;
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace,
+                   workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_fused_gemv_quant(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
+                           int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
+                           float* sx_out, void* workspace, size_t workspace_bytes,
+                           fp8gq_stream_t stream) {
+  if (M == 1 && K <= kRowMaxK) {
+    int st = check_common(x, w, ws, out, M, N, K, ldw, ldws, ldo);
+    if (st != FP8GQ_OK) return st;
+    return launch_row(false, x, w, ldw, ws, ldws, out, N, K, xq_out, sx_out,
+                      static_cast<cudaStream_t>(stream));
+  }
+  return fp8gq_gemv_quant_tm(x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace,
+                             workspace_bytes, stream);
+}
+
+int fp8gq_fused_swiglu_q_gemm(const void* gu, int64_t ldgu, const void* w, int64_t ldw,
+                              const float* ws, int64_t ldws, void* out, int64_t ldo, int M, int N,
+                              int I, uint8_t* xq_out, float* sx_out, void* workspace,
+                              size_t workspace_bytes, fp8gq_stream_t stream) {
+  int st = check_common(gu, w, ws, out, M, N, I, ldw, ldws, ldo);
+  if (st != FP8GQ_OK) return st;
+  if (ldgu < 2 * static_cast<int64_t>(I)) return FP8GQ_ERR_STRIDE;
+  if (ldgu % 8) return FP8GQ_ERR_ALIGNMENT;
+  if (M == 1 && I <= kRowMaxK)
+    return launch_row(true, gu, w, ldw, ws, ldws, out, N, I, xq_out, sx_out,
+                      static_cast<cudaStream_t>(stream));
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  return launch_tm(true, gu, ldgu, w, ldw, ws, ldws, out, ldo, M, N, I, xq_out, sx_out, workspace,
+                   workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_group_quant(const void* x, int64_t ldx, int M, int K, uint8_t* xq, float* sx,
+                      fp8gq_stream_t stream) {
+  if (!x || !xq || !sx) return FP8GQ_ERR_NULL_POINTER;
+  if (M < 1 || K <= 0 || K % kGroup) return FP8GQ_ERR_SHAPE;
+  if (ldx < K) return FP8GQ_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(x) & 7u) || (ldx % 4) || (reinterpret_cast<uintptr_t>(xq) & 3u) ||
+      (reinterpret_cast<uintptr_t>(sx) & 3u))
+    return FP8GQ_ERR_ALIGNMENT;
+  return launch_quant(false, x, ldx, M, K, xq, sx, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_swiglu_group_quant(const void* gu, int64_t ldgu, int M, int I, uint8_t* xq, float* sx,
+                             fp8gq_stream_t stream) {
+  if (!gu || !xq || !sx) return FP8GQ_ERR_NULL_POINTER;
+  if (M < 1 || I <= 0 || I % kGroup) return FP8GQ_ERR_SHAPE;
+  if (ldgu < 2 * static_cast<int64_t>(I)) return FP8GQ_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(gu) & 7u) || (ldgu % 4) || (reinterpret_cast<uintptr_t>(xq) & 3u) ||
+      (reinterpret_cast<uintptr_t>(sx) & 3u))
+    return FP8GQ_ERR_ALIGNMENT;
+  return launch_quant(true, gu, ldgu, M, I, xq, sx, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_device_error(uint32_t* code, int clear) {
+  if (!code) return FP8GQ_ERR_NULL_POINTER;
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  *code = v;
+  if (clear && v) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  }
+  return FP8GQ_OK;
+}
+
+}  // extern "C"

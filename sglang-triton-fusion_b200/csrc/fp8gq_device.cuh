@@ -1,0 +1,195 @@
+// Device-side building blocks shared by the fp8gq kernels (sm_100a):
+// the activation group quant, the SwiGLU prologue, e4m3/f16 conversions,
+// mbarriers and 1-D bulk (TMA) copies with bounded waits.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+namespace fp8gq {
+
+constexpr int kGroup = 128;          // 1x128 activation groups, 128x128 weight blocks
+constexpr float kE4m3Max = 448.0f;   // largest finite e4m3fn value
+constexpr float kEps = 1e-10f;       // amax floor (kernels/fused_gemv_quant_tm.py:144)
+
+// Error word written when a bounded wait gives up (read by fp8gq_device_error).
+// Low 16 bits: site id; bit 31: set.  libfp8gq is one translation unit
+// (fp8gq_api.cu), which is where this definition lands.
+__device__ unsigned int g_device_error = 0;
+
+enum ErrorSite : unsigned int {
+  kSiteRowFull = 1,      // row kernel consumer waiting for a weight stage
+  kSiteRowEmpty = 2,     // row kernel producer waiting for a free stage
+  kSiteTmA = 3,          // tile kernel waits (A/B/accumulator/TMEM rings)
+  kSiteTmB = 4,
+  kSiteTmAcc = 5,
+  kSiteTmTmem = 6,
+  kSiteTmFixup = 7,      // tile kernel split-K partial-sum hand-off
+};
+
+__device__ __forceinline__ void record_error(unsigned int site) {
+  atomicCAS(&g_device_error, 0u, 0x80000000u | site);
+}
+
+// ---------------------------------------------------------------------------
+// timing for bounded waits
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Give up after ~2 s: every wait in these kernels is for work of the same CTA
+// (or the same grid) that completes in microseconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ---------------------------------------------------------------------------
+// mbarrier + 1-D bulk copy (TMA, no tensor map, no multicast)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete; false (and the error
+// word set) if that takes longer than kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0u && global_ns() - t0 > kWaitLimitNs) {
+      record_error(site);
+      return false;
+    }
+  }
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// global to this CTA's shared memory; completion is counted on `bar`.  The
+// weight stream is read once, so it is marked evict-first in L2.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar, uint64_t l2_policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(l2_policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// activation quant (sglang formula, bit-exact with the oracle)
+// ---------------------------------------------------------------------------
+
+// Scale of a group from its max |value|: amax floored at 1e-10, IEEE division
+// by 448 (kernels/fused_gemv_quant.py:40-41).
+__device__ __forceinline__ float group_scale(float amax) {
+  return __fdiv_rn(fmaxf(amax, kEps), kE4m3Max);
+}
+
+// Two fp32 values -> two e4m3 codes (v0 in the low byte): y = v * (1/sx)
+// (IEEE multiply), clamp to +-448, round to nearest even
+// (kernels/fused_gemv_quant.py:42-43).
+__device__ __forceinline__ uint16_t quant_pair(float v0, float v1, float sinv) {
+  float y0 = fminf(fmaxf(__fmul_rn(v0, sinv), -kE4m3Max), kE4m3Max);
+  float y1 = fminf(fmaxf(__fmul_rn(v1, sinv), -kE4m3Max), kE4m3Max);
+  return static_cast<uint16_t>(__nv_cvt_float2_to_fp8x2(make_float2(y0, y1), __NV_SATFINITE, __NV_E4M3));
+}
+
+// Two e4m3 codes (low byte first) -> f16x2 (exact: every e4m3 value is an f16).
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t two) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// ---------------------------------------------------------------------------
+// SwiGLU prologue: act = (g * sigmoid(g)) * u, sigmoid(g) = 1 / (1 + exp(-g))
+// (kernels/fused_swiglu_quant_gemv.py:40-42).  exp is evaluated by the
+// Cody-Waite reduction and the degree-5 minimax polynomial published in the
+// Cephes library (S. L. Moshier, expf.c), one rounded fp32 operation per
+// step and no fused multiply-add, so the CPU oracle evaluates the identical
+// sequence and the quantised bytes agree bit for bit.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float exp_cw(float x) {
+  const float kLog2e = 1.44269504088896341f;
+  const float kC1 = 0.693359375f;
+  const float kC2 = -2.12194440e-4f;
+  if (x != x) return x;
+  if (x > 88.0f) return __int_as_float(0x7f800000);
+  if (x < -88.0f) return 0.0f;
+  const float n = rintf(__fmul_rn(x, kLog2e));
+  float r = __fsub_rn(x, __fmul_rn(n, kC1));
+  r = __fsub_rn(r, __fmul_rn(n, kC2));
+  float p = 1.9875691500e-4f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.3981999507e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 8.3334519073e-3f);
+  p = __fadd_rn(__fmul_rn(p, r), 4.1665795894e-2f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.6666665459e-1f);
+  p = __fadd_rn(__fmul_rn(p, r), 5.0000001201e-1f);
+  p = __fmul_rn(p, __fmul_rn(r, r));
+  p = __fadd_rn(p, r);
+  p = __fadd_rn(p, 1.0f);
+  const int ni = static_cast<int>(n);
+  const int h1 = (ni >= 0) ? (ni / 2) : -((-ni + 1) / 2);  // floor(n / 2)
+  const int h2 = ni - h1;
+  const float s1 = __int_as_float((h1 + 127) << 23);
+  const float s2 = __int_as_float((h2 + 127) << 23);
+  return __fmul_rn(__fmul_rn(p, s1), s2);
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  const float e = exp_cw(-g);
+  const float s = __frcp_rn(__fadd_rn(1.0f, e));
+  return __fmul_rn(__fmul_rn(g, s), u);
+}
+
+}  // namespace fp8gq

@@ -1,0 +1,307 @@
+// M == 1 fused quant + GEMV on CUDA cores (replaces gemv_quant_row_kernel,
+// kernels/fused_gemv_quant_tm.py:25-46, and swiglu_q_gemm_kernel at M == 1,
+// kernels/fused_swiglu_quant_gemv.py:26-51).
+//
+// Work split.  The N weight rows are cut into row groups of R rows; CTA i of
+// G owns the contiguous row groups [i*NG/G, (i+1)*NG/G), so every CTA streams
+// one contiguous slice of W and computes whole dot products: no split-K, no
+// scratch memory, one bf16 store per row.
+//
+// Pipeline.  One producer warp issues 1-D bulk copies (TMA) of R rows
+// (R*K bytes) into a ring of shared-memory stages; `full[s]` counts the bytes,
+// `empty[s]` counts the consumer warps that are done with the stage.
+//
+// Consumers.  T threads (T % 32 == 0) split K: thread t owns the 16-byte
+// column chunks t, t+T, ..., t+(C-1)T, i.e. the same K positions in every
+// row, so its slice of the quantised activation is computed once and kept in
+// registers (as f16 pairs: every e4m3 value is exact in f16).  For each row it
+// forms 16-product partial sums per chunk with fp32 accumulation
+// (fma.rn.f32.f16: products are exact), scales each by sx[b] * ws[n/128, b]
+// -- all 16 columns of a chunk lie in one 128-block b -- and sums; a warp
+// butterfly reduces the R rows at once, and per-warp row sums go through a
+// double-buffered 32-row window in shared memory where warp 0 adds them up
+// and stores bf16.
+#pragma once
+
+#include "fp8gq_device.cuh"
+
+namespace fp8gq {
+
+struct RowParams {
+  const __nv_bfloat16* x;   // [K] (plain) or [2K] = [gate | up] (SwiGLU)
+  const uint8_t* w;         // [N, ldw] e4m3
+  int64_t ldw;
+  const float* ws;          // [N/128, ldws]
+  int64_t ldws;
+  __nv_bfloat16* out;       // [N]
+  int N, K;
+  int n_groups;             // N / R
+  int stages;               // ring depth
+  uint8_t* xq_out;          // optional [K]
+  float* sx_out;            // optional [K/128]
+};
+
+constexpr int kRowMaxConsumerThreads = 384;  // the launcher never picks T > 384
+constexpr int kRowWindow = 32;  // rows per reduction window
+
+// Shared-memory layout after the ring: full[stages], empty[stages],
+// window[2][n_consumer_warps][32] fp32.
+__host__ __device__ inline size_t row_smem_bytes(int stages, int stage_bytes, int n_cwarps) {
+  size_t ring = static_cast<size_t>(stages) * stage_bytes;
+  size_t bars = static_cast<size_t>(2 * stages) * sizeof(uint64_t);
+  size_t win = static_cast<size_t>(2 * n_cwarps * kRowWindow) * sizeof(float);
+  return ring + bars + win;
+}
+
+// Sum of 16 exact products xq[k] * w[k] in fp32 (two accumulators).
+__device__ __forceinline__ float dot16_e4m3(const uint4 wv, const uint32_t (&xh)[8]) {
+  float a0 = 0.0f, a1 = 0.0f;
+  const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t wlo = e4m3x2_to_f16x2(static_cast<uint16_t>(words[q] & 0xFFFFu));
+    const uint32_t whi = e4m3x2_to_f16x2(static_cast<uint16_t>(words[q] >> 16));
+    asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+        "mov.b32 {w0, w1}, %2;\n\t"
+        "mov.b32 {x0, x1}, %3;\n\t"
+        "fma.rn.f32.f16 %0, w0, x0, %0;\n\t"
+        "fma.rn.f32.f16 %1, w1, x1, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(wlo), "r"(xh[2 * q]));
+    asm("{\n\t.reg .b16 w0, w1, x0, x1;\n\t"
+        "mov.b32 {w0, w1}, %2;\n\t"
+        "mov.b32 {x0, x1}, %3;\n\t"
+        "fma.rn.f32.f16 %0, w0, x0, %0;\n\t"
+        "fma.rn.f32.f16 %1, w1, x1, %1;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "r"(whi), "r"(xh[2 * q + 1]));
+  }
+  return a0 + a1;
+}
+
+// Butterfly over the warp that reduces R per-lane values at once.  Returns
+// the full warp sum of row `row_of_lane(lane)` in every lane.
+template <int R>
+__device__ __forceinline__ float warp_reduce_rows(float (&v)[R], int lane) {
+  int n = R;
+  int off = 16;
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    if (n > 1) {
+      const int half = n / 2;
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int k = 0; k < R / 2; ++k) {
+        if (k < half) {
+          const float send = up ? v[k] : v[k + half];
+          const float keep = up ? v[k + half] : v[k];
+          v[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+    off >>= 1;
+  }
+  return v[0];
+}
+
+template <int R>
+__device__ __forceinline__ int row_of_lane(int lane) {
+  int row = 0, n = R, off = 16;
+#pragma unroll
+  for (int step = 0; step < 5; ++step) {
+    if (n > 1) {
+      const int half = n / 2;
+      if (lane & off) row += half;
+      n = half;
+    }
+    off >>= 1;
+  }
+  return row;
+}
+
+template <int C, int R, bool kSwiglu>
+__global__ void __launch_bounds__(kRowMaxConsumerThreads + 32, 1)
+gemv_row_kernel(const RowParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int stage_bytes = R * p.K;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + static_cast<size_t>(p.stages) * stage_bytes);
+  uint64_t* empty = full + p.stages;
+  const int n_cwarps = blockDim.x / 32 - 1;
+  const int T = n_cwarps * 32;
+  float* window = reinterpret_cast<float*>(empty + p.stages);  // [2][n_cwarps][32]
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  const int g0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.n_groups) / gridDim.x);
+  const int g1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.n_groups) / gridDim.x);
+  const int n_my = g1 - g0;
+
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], n_cwarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ producer --
+  if (warp == n_cwarps) {
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_first();
+      for (int j = 0; j < n_my; ++j) {
+        const int s = j % p.stages;
+        if (j >= p.stages) {
+          if (!mbar_wait(&empty[s], ((j / p.stages) & 1) ^ 1, kSiteRowEmpty)) break;
+        }
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
+        const int64_t row0 = static_cast<int64_t>(g0 + j) * R;
+        uint8_t* dst = smem + static_cast<size_t>(s) * stage_bytes;
+        if (p.ldw == p.K) {
+          bulk_g2s(dst, p.w + row0 * p.K, static_cast<uint32_t>(stage_bytes), &full[s], pol);
+        } else {
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+            bulk_g2s(dst + r * p.K, p.w + (row0 + r) * p.ldw, static_cast<uint32_t>(p.K), &full[s], pol);
+        }
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------------------- consumers: prologue --
+  // Quantise this thread's chunks of the activation (whole 128-groups are
+  // shared by 8 consecutive lanes, so the group amax is a 3-step shuffle).
+  const int n_chunks = p.K / 16;
+  uint32_t xh[C][8];
+  float sx_c[C];
+  int blk[C];
+#pragma unroll
+  for (int i = 0; i < C; ++i) {
+    const int c = tid + T * i;
+    const bool valid = c < n_chunks;
+    float v[16];
+    if (valid) {
+      if constexpr (kSwiglu) {
+        const uint4* gp = reinterpret_cast<const uint4*>(p.x + 16 * c);
+        const uint4* up = reinterpret_cast<const uint4*>(p.x + p.K + 16 * c);
+        const uint4 g_a = gp[0], g_b = gp[1], u_a = up[0], u_b = up[1];
+        const uint32_t gw[8] = {g_a.x, g_a.y, g_a.z, g_a.w, g_b.x, g_b.y, g_b.z, g_b.w};
+        const uint32_t uw[8] = {u_a.x, u_a.y, u_a.z, u_a.w, u_b.x, u_b.y, u_b.z, u_b.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          v[2 * e] = silu_mul(bf16_lo(gw[e]), bf16_lo(uw[e]));
+          v[2 * e + 1] = silu_mul(bf16_hi(gw[e]), bf16_hi(uw[e]));
+        }
+      } else {
+        const uint4* xp = reinterpret_cast<const uint4*>(p.x + 16 * c);
+        const uint4 a = xp[0], b = xp[1];
+        const uint32_t xw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          v[2 * e] = bf16_lo(xw[e]);
+          v[2 * e + 1] = bf16_hi(xw[e]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    const float sx = group_scale(amax);
+    const float sinv = __frcp_rn(sx);
+    uint16_t q[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      q[e] = quant_pair(v[2 * e], v[2 * e + 1], sinv);
+      xh[i][e] = e4m3x2_to_f16x2(q[e]);
+    }
+    sx_c[i] = sx;
+    blk[i] = c >> 3;
+    if (valid && blockIdx.x == 0) {
+      if (p.xq_out) {
+        uint4 packed;
+        packed.x = q[0] | (static_cast<uint32_t>(q[1]) << 16);
+        packed.y = q[2] | (static_cast<uint32_t>(q[3]) << 16);
+        packed.z = q[4] | (static_cast<uint32_t>(q[5]) << 16);
+        packed.w = q[6] | (static_cast<uint32_t>(q[7]) << 16);
+        *reinterpret_cast<uint4*>(p.xq_out + 16 * c) = packed;
+      }
+      if (p.sx_out && (c & 7) == 0) p.sx_out[c >> 3] = sx;
+    }
+  }
+
+  // ------------------------------------------------ consumers: main loop --
+  const int row_begin = g0 * R;
+  const int rows_my = n_my * R;
+  float s_cur[C];
+  int nb_cur = -1;
+  bool ok = true;
+  int win_buf = 0;
+  const int my_row_in_group = row_of_lane<R>(lane);
+  const bool row_writer = (lane & ((32 / R) - 1)) == 0;
+
+  for (int j = 0; j < n_my; ++j) {
+    const int s = j % p.stages;
+    if (ok) ok = mbar_wait(&full[s], (j / p.stages) & 1, kSiteRowFull);
+    const int row0 = row_begin + j * R;
+    const int nb = row0 >> 7;
+    if (nb != nb_cur) {
+      nb_cur = nb;
+#pragma unroll
+      for (int i = 0; i < C; ++i) {
+        const int c = tid + T * i;
+        s_cur[i] = (c < n_chunks) ? sx_c[i] * __ldg(p.ws + static_cast<int64_t>(nb) * p.ldws + blk[i]) : 0.0f;
+      }
+    }
+    float acc[R];
+    const uint8_t* stage = smem + static_cast<size_t>(s) * stage_bytes;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      acc[r] = 0.0f;
+#pragma unroll
+      for (int i = 0; i < C; ++i) {
+        const int c = tid + T * i;
+        if (c < n_chunks && ok) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(stage + r * p.K + 16 * c);
+          acc[r] = fmaf(dot16_e4m3(wv, xh[i]), s_cur[i], acc[r]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    const float rs = warp_reduce_rows<R>(acc, lane);
+    const int row_in_win = (j * R) % kRowWindow;
+    float* win = window + (win_buf * n_cwarps) * kRowWindow;
+    if (row_writer) win[warp * kRowWindow + row_in_win + my_row_in_group] = rs;
+
+    const int done_rows = (j + 1) * R;
+    if (done_rows % kRowWindow == 0 || j == n_my - 1) {
+      named_bar_sync(1, T);
+      if (warp == 0) {
+        const int wrow0 = ((done_rows - 1) / kRowWindow) * kRowWindow;
+        const int nrows = done_rows - wrow0;
+        if (lane < nrows) {
+          float sum = 0.0f;
+          for (int w = 0; w < n_cwarps; ++w) sum += win[w * kRowWindow + lane];
+          p.out[row_begin + wrow0 + lane] = __float2bfloat16_rn(sum);
+        }
+      }
+      win_buf ^= 1;
+    }
+  }
+  (void)rows_my;
+}
+
+}  // namespace fp8gq

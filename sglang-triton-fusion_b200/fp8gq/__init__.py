@@ -1,0 +1,17 @@
+"""fp8gq: fused FP8 (e4m3) activation group-quant + block-scaled GEMV for
+NVIDIA B200 (sm_100a), behind the drop-in surface of the sglang patch
+``patches/patch_fp8_fused_tail.py`` of wafik/sglang-triton-fusion.
+
+Entry points:
+  fused_gemv_quant(x, Wq, Ws)      M == 1 row kernel / M > 1 tcgen05 tile kernel
+  fused_swiglu_q_gemm(gu, Wd, Ws)  SwiGLU + quant + down_proj GEMV
+  group_quant(x), swiglu_group_quant(gu)   the activation quant alone
+  patch_fp8_fused_tail             the sglang linear wrappers and install()
+The C ABI is include/fp8gq.h (libfp8gq.so next to this file).
+"""
+from ._lib import Fp8gqError, device_error, load  # noqa: F401
+from .ops import (GROUP, TM, ShapeError, fused_gemv_quant, fused_swiglu_q_gemm,  # noqa: F401
+                  group_quant, swiglu_group_quant, workspace)
+
+__all__ = ["Fp8gqError", "ShapeError", "GROUP", "TM", "fused_gemv_quant", "fused_swiglu_q_gemm",
+           "group_quant", "swiglu_group_quant", "workspace", "load", "device_error"]

@@ -1,0 +1,101 @@
+"""ctypes binding of libfp8gq.so (include/fp8gq.h).
+
+There is no fallback: if the library cannot be loaded, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from . import _build
+
+_lock = threading.Lock()
+_lib = None
+
+STATUS = {
+    0: "FP8GQ_OK",
+    1: "FP8GQ_ERR_NULL_POINTER",
+    2: "FP8GQ_ERR_SHAPE",
+    3: "FP8GQ_ERR_ALIGNMENT",
+    4: "FP8GQ_ERR_STRIDE",
+    5: "FP8GQ_ERR_WORKSPACE",
+    6: "FP8GQ_ERR_DEVICE",
+    7: "FP8GQ_ERR_LAUNCH",
+    8: "FP8GQ_ERR_UNSUPPORTED",
+    9: "FP8GQ_ERR_DEVICE_TIMEOUT",
+}
+
+# name -> (restype, argtypes); the order of include/fp8gq.h
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_I64 = ctypes.c_int64
+_SZ = ctypes.c_size_t
+SIGNATURES = {
+    "fp8gq_version": (_I, []),
+    "fp8gq_status_string": (ctypes.c_char_p, [_I]),
+    "fp8gq_fused_gemv_quant": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
+    "fp8gq_workspace_bytes": (_SZ, [_I, _I, _I]),
+    "fp8gq_gemv_quant_row": (_I, [_P, _P, _I64, _P, _I64, _P, _I, _I, _P, _P, _P]),
+    "fp8gq_gemv_quant_tm": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
+    "fp8gq_fused_swiglu_q_gemm": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
+    "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
+    "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+}
+
+
+class Fp8gqError(RuntimeError):
+    """A libfp8gq entry point returned a non-zero status."""
+
+    def __init__(self, status: int, what: str):
+        self.status = status
+        super().__init__(f"{what}: {STATUS.get(status, status)} ({status_string(status)})")
+
+
+def library_path() -> Path:
+    return _build.LIB_PATH
+
+
+def load(build_if_missing: bool = True):
+    """Load (building first when the .so is missing or stale and nvcc exists)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB_PATH
+        if build_if_missing and not _build.up_to_date():
+            try:
+                _build.build()
+            except RuntimeError:
+                if not path.exists():
+                    raise
+        if not path.exists():
+            raise RuntimeError(f"{path} is missing: build it with `python -m fp8gq._build`")
+        lib = ctypes.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    lib = _lib
+    if lib is None:
+        return STATUS.get(status, "unknown")
+    return lib.fp8gq_status_string(status).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise Fp8gqError(status, what)
+
+
+def device_error(clear: bool = False) -> int:
+    """Error word set by a kernel whose bounded wait gave up (0 = none)."""
+    lib = load()
+    code = ctypes.c_uint32(0)
+    check(lib.fp8gq_device_error(ctypes.byref(code), 1 if clear else 0), "fp8gq_device_error")
+    return int(code.value)

@@ -1,0 +1,172 @@
+"""torch-tensor front end of libfp8gq: checks dtypes and layouts, allocates
+the output from torch's caching allocator (as the reference wrapper does,
+kernels/fused_gemv_quant_tm.py:89) and launches on torch's current stream.
+
+Every op runs the CUDA kernels; there is no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+GROUP = 128
+TM = 16  # largest M routed to the fused kernels by the patch layer
+
+
+class ShapeError(AssertionError, ValueError):
+    """Shape the fused path does not take (the reference asserts the same:
+    kernels/fused_gemv_quant_tm.py:87)."""
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_workspaces: dict = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """Zero-filled scratch kept per (device, stream).  The kernels leave it
+    zero-filled when they finish, so it is allocated and cleared once; grow it
+    (and warm every shape up) before capturing a CUDA graph."""
+    stream = _stream(device)
+    key = (device.index, stream)
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
+def _check_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("fp8gq ops take CUDA tensors only (there is no CPU path)")
+
+
+def _check_weight(Wq: torch.Tensor, Ws: torch.Tensor, K: int):
+    if Wq.dtype != torch.float8_e4m3fn:
+        raise TypeError(f"weight must be float8_e4m3fn, got {Wq.dtype}")
+    if Ws.dtype != torch.float32:
+        raise TypeError(f"weight_scale must be float32, got {Ws.dtype}")
+    N, Kw = Wq.shape
+    if Kw != K:
+        raise ShapeError(f"weight has K={Kw}, activation has K={K}")
+    if K % GROUP or N % GROUP:
+        raise ShapeError("K and N must be multiples of 128")
+    if Wq.stride(1) != 1 or Ws.stride(1) != 1:
+        raise ValueError("weight and weight_scale must be contiguous along K")
+    if tuple(Ws.shape) != (N // GROUP, K // GROUP):
+        raise ShapeError(f"weight_scale must be [{N // GROUP}, {K // GROUP}], got {tuple(Ws.shape)}")
+    return N
+
+
+def _quant_out(M, K, device, want):
+    if not want:
+        return None, None
+    return (torch.empty(M, K, dtype=torch.uint8, device=device),
+            torch.empty(M, K // GROUP, dtype=torch.float32, device=device))
+
+
+def fused_gemv_quant(x: torch.Tensor, Wq: torch.Tensor, Ws: torch.Tensor, *, out=None,
+                     return_quant: bool = False, kernel: str = "auto"):
+    """x: (M, K) bf16; Wq: (N, K) e4m3; Ws: (N/128, K/128) fp32 -> (M, N) bf16.
+
+    Same contract as fused_gemv_quant (kernels/fused_gemv_quant_tm.py:83-102):
+    M == 1 runs the row kernel, M > 1 the tensor-core tile kernel.
+    ``kernel`` = "row" or "tm" forces one of them; ``return_quant`` also
+    returns the quantised activation bytes (uint8 e4m3 codes) and scales that
+    the kernel computed internally."""
+    _check_cuda(x, Wq, Ws)
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise TypeError("x must be a 2-D bf16 tensor")
+    M, K = x.shape
+    N = _check_weight(Wq, Ws, K)
+    if x.stride(1) != 1:
+        raise ValueError("x must be contiguous along K")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    xq, sx = _quant_out(M, K, x.device, return_quant)
+    lib = _lib.load()
+    stream = _stream(x.device)
+    if kernel == "row":
+        if M != 1:
+            raise ShapeError("the row kernel takes M == 1")
+        st = lib.fp8gq_gemv_quant_row(_ptr(x), _ptr(Wq), Wq.stride(0), _ptr(Ws), Ws.stride(0), _ptr(out),
+                                      N, K, _ptr(xq), _ptr(sx), stream)
+        _lib.check(st, "fp8gq_gemv_quant_row")
+    else:
+        nbytes = lib.fp8gq_workspace_bytes(M, N, K) if kernel == "auto" else _tm_ws_bytes(lib, M, N, K)
+        ws_buf = workspace(x.device, nbytes) if nbytes else None
+        fn = lib.fp8gq_fused_gemv_quant if kernel == "auto" else lib.fp8gq_gemv_quant_tm
+        if kernel not in ("auto", "tm"):
+            raise ValueError(f"unknown kernel {kernel!r}")
+        st = fn(_ptr(x), x.stride(0), _ptr(Wq), Wq.stride(0), _ptr(Ws), Ws.stride(0), _ptr(out), out.stride(0),
+                M, N, K, _ptr(xq), _ptr(sx), _ptr(ws_buf), 0 if ws_buf is None else ws_buf.numel(), stream)
+        _lib.check(st, fn.__name__)
+    return (out, xq, sx) if return_quant else out
+
+
+def _tm_ws_bytes(lib, M, N, K):
+    # the tile kernel's scratch, also for M == 1 (which "auto" sends to the row kernel)
+    return lib.fp8gq_workspace_bytes(max(M, 2), N, K)
+
+
+def fused_swiglu_q_gemm(gu: torch.Tensor, Wd: torch.Tensor, Ws: torch.Tensor, *, out=None,
+                        return_quant: bool = False):
+    """gu: (M, 2I) bf16 gate_up output ([gate | up]); Wd: (N, I) e4m3;
+    Ws: (N/128, I/128) fp32 -> (M, N) bf16
+    (kernels/fused_swiglu_quant_gemv.py:54-67)."""
+    _check_cuda(gu, Wd, Ws)
+    if gu.dtype != torch.bfloat16 or gu.dim() != 2:
+        raise TypeError("gu must be a 2-D bf16 tensor")
+    M, two_i = gu.shape
+    if two_i % 2:
+        raise ShapeError("gu must have an even number of columns ([gate | up])")
+    I = two_i // 2
+    N = _check_weight(Wd, Ws, I)
+    if gu.stride(1) != 1:
+        raise ValueError("gu must be contiguous along its last dimension")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=gu.device)
+    xq, sx = _quant_out(M, I, gu.device, return_quant)
+    lib = _lib.load()
+    nbytes = lib.fp8gq_workspace_bytes(M, N, I)
+    ws_buf = workspace(gu.device, nbytes) if nbytes else None
+    st = lib.fp8gq_fused_swiglu_q_gemm(_ptr(gu), gu.stride(0), _ptr(Wd), Wd.stride(0), _ptr(Ws), Ws.stride(0),
+                                       _ptr(out), out.stride(0), M, N, I, _ptr(xq), _ptr(sx), _ptr(ws_buf),
+                                       0 if ws_buf is None else ws_buf.numel(), _stream(gu.device))
+    _lib.check(st, "fp8gq_fused_swiglu_q_gemm")
+    return (out, xq, sx) if return_quant else out
+
+
+def group_quant(x: torch.Tensor):
+    """x: (M, K) bf16 -> (xq uint8 e4m3 codes (M, K), sx fp32 (M, K/128))."""
+    _check_cuda(x)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+        raise TypeError("x must be a 2-D bf16 tensor, contiguous along K")
+    M, K = x.shape
+    xq, sx = _quant_out(M, K, x.device, True)
+    lib = _lib.load()
+    _lib.check(lib.fp8gq_group_quant(_ptr(x), x.stride(0), M, K, _ptr(xq), _ptr(sx), _stream(x.device)),
+               "fp8gq_group_quant")
+    return xq, sx
+
+
+def swiglu_group_quant(gu: torch.Tensor):
+    """gu: (M, 2I) bf16 -> (xq (M, I), sx (M, I/128)) of silu(gate) * up."""
+    _check_cuda(gu)
+    if gu.dtype != torch.bfloat16 or gu.dim() != 2 or gu.stride(1) != 1:
+        raise TypeError("gu must be a 2-D bf16 tensor, contiguous along its last dimension")
+    M, two_i = gu.shape
+    I = two_i // 2
+    xq, sx = _quant_out(M, I, gu.device, True)
+    lib = _lib.load()
+    _lib.check(lib.fp8gq_swiglu_group_quant(_ptr(gu), gu.stride(0), M, I, _ptr(xq), _ptr(sx),
+                                            _stream(gu.device)), "fp8gq_swiglu_group_quant")
+    return xq, sx

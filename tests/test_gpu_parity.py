@@ -1,0 +1,264 @@
+"""Parity of the CUDA kernels (through the C ABI, via fp8gq.ops) against the
+CPU oracle: quantised activation bytes and scales bit-exact, outputs within
+the north star's tolerance (rtol 1e-2, atol 1e-2 * RMS) and within the
+reference self-tests' ulp tolerance (2 bf16 ulp + 1e-3 for the row and
+SwiGLU kernels, kernels/fused_gemv_quant.py:107-108; 3 ulp + 1e-3 for the
+tile kernel, kernels/fused_gemv_quant_tm.py:138-140)."""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fp8gq_oracle as O
+from tests._util import (assert_close, bf16_bits_tensor, bf16_tensor, f32_tensor, fp8_tensor, to_f32,
+                         to_u8)
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+
+# Qwen3-8B decode linears (K, N) and Qwen3-4B tile shapes
+QWEN3_8B = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 24576), "down": (12288, 4096)}
+QWEN3_4B = {"q": (2560, 4096), "gate_up": (2560, 19456), "down": (9728, 2560)}
+
+
+@pytest.fixture(scope="module")
+def fp8gq(cuda_device):
+    import fp8gq as mod
+    mod.load()
+    return mod
+
+
+def gpu_weight(N, K, seed, dev):
+    """Seeded e4m3 weight [N, K] with 128x128 block scales, made on the GPU
+    (N(0, 0.02^2) in bf16, ws = amax/448, RNE cast)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = (torch.randn(N, K, generator=g, device=dev) * 0.02).bfloat16().float()
+    blk = w.view(N // 128, 128, K // 128, 128)
+    ws = blk.abs().amax(dim=(1, 3)).clamp_min(1e-10) / 448.0
+    q = (blk / ws[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(N, K)
+    return q.contiguous(), ws.contiguous()
+
+
+def gpu_activation(M, K, seed, dev, std=1.0, outliers=True):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(M, K, generator=g, device=dev) * std
+    if outliers:
+        ch = torch.randperm(K, generator=g, device=dev)[: max(1, round(0.01 * K))]
+        x[:, ch] *= 20.0
+    return x.bfloat16().contiguous()
+
+
+def oracle_of(x, wq, ws, swiglu=False):
+    fn = O.fused_swiglu_q_gemm if swiglu else O.fused_gemv_quant
+    return fn(to_f32(x), to_u8(wq), to_f32(ws))
+
+
+# ---------------------------------------------------------------- quant --
+
+@pytest.mark.parametrize("M, K", [(1, 4096), (16, 2560), (3, 12288), (5, 128)])
+def test_group_quant_bit_exact(fp8gq, cuda_device, M, K):
+    x = gpu_activation(M, K, 100 + M, cuda_device)
+    xq, sx = fp8gq.group_quant(x)
+    rq, rs = O.group_quant(to_f32(x))
+    assert np.array_equal(to_u8(xq), rq)
+    assert np.array_equal(to_f32(sx), rs)
+
+
+def test_group_quant_special_values(fp8gq, cuda_device):
+    x = np.zeros((2, 640), np.float32)
+    x[0, 128:256] = 3.0
+    x[0, 130] = -400.0                                     # saturates to -448
+    x[0, 256:384] = np.linspace(-1e-3, 1e-3, 128)           # subnormal codes and signed zeros
+    x[0, 300] = 1.0
+    x[0, 384:512] = 1e30                                     # huge but finite in bf16
+    x[1, :] = np.float32(2.0) ** -120                        # tiny: below the eps floor
+    x[1, 512:640] = -0.0
+    x = O.bf16_round(x)
+    xt = bf16_tensor(x, cuda_device)
+    xq, sx = fp8gq.group_quant(xt)
+    rq, rs = O.group_quant(x)
+    assert np.array_equal(to_u8(xq), rq)
+    assert np.array_equal(to_f32(sx), rs)
+    assert to_u8(xq)[0, 130] == 0xFE
+
+
+@pytest.mark.parametrize("M, I", [(1, 12288), (4, 2560)])
+def test_swiglu_group_quant_bit_exact(fp8gq, cuda_device, M, I):
+    gu = gpu_activation(M, 2 * I, 7, cuda_device, std=1.5, outliers=False)
+    gu[:, :64] = -50.0           # silu -> ~0, stays finite
+    gu[:, 64:128] = 20.0
+    gu[:, I + 64:I + 128] = 20.0  # silu(20) * 20 = 400 -> group max at 448
+    xq, sx = fp8gq.swiglu_group_quant(gu)
+    rq, rs, _ = O.swiglu_quant(to_f32(gu))
+    assert np.array_equal(to_u8(xq), rq)
+    assert np.array_equal(to_f32(sx), rs)
+
+
+# ------------------------------------------------------- golden fixtures --
+
+@pytest.mark.parametrize("path", GOLDEN, ids=[p.stem for p in GOLDEN])
+def test_golden_fixtures(fp8gq, cuda_device, path):
+    """Every golden case through the routed entry point (M == 1 -> row
+    kernel, M > 1 -> tile kernel), against the reference kernels' own output."""
+    d = np.load(path)
+    x = bf16_bits_tensor(d["x_bf16"], cuda_device)
+    wq = fp8_tensor(d["wq"], cuda_device)
+    ws = f32_tensor(d["ws"], cuda_device)
+    swiglu = str(d["kind"]) == "swiglu"
+    fn = fp8gq.fused_swiglu_q_gemm if swiglu else fp8gq.fused_gemv_quant
+    out, xq, sx = fn(x, wq, ws, return_quant=True)
+    ref_out, exact, rq, rs = oracle_of(x, wq, ws, swiglu)
+    assert np.array_equal(to_u8(xq), rq), "quantised bytes differ from the oracle"
+    assert np.array_equal(to_f32(sx), rs), "scales differ from the oracle"
+    golden = O.bf16_from_bits(d["out_bf16"])
+    ulps = 2.0 if x.shape[0] == 1 else 3.0
+    assert_close(to_f32(out), exact, ulps)
+    assert np.max(np.abs(to_f32(out) - golden)) <= O.ref_atol(golden, ulps)
+
+
+# ------------------------------------------------------------ row kernel --
+
+@pytest.mark.parametrize("name", list(QWEN3_8B))
+def test_row_kernel_qwen3_8b(fp8gq, cuda_device, name):
+    K, N = QWEN3_8B[name]
+    x = gpu_activation(1, K, 1, cuda_device)
+    wq, ws = gpu_weight(N, K, 2, cuda_device)
+    out, xq, sx = fp8gq.fused_gemv_quant(x, wq, ws, return_quant=True)
+    _, exact, rq, rs = oracle_of(x, wq, ws)
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert_close(to_f32(out), exact, 2.0)
+
+
+@pytest.mark.parametrize("K, N", [(128, 128), (256, 384), (2560, 4096), (9728, 2560), (1152, 1280),
+                                  (16384, 512), (49152, 256)])
+def test_row_kernel_shapes(fp8gq, cuda_device, K, N):
+    x = gpu_activation(1, K, K + N, cuda_device)
+    wq, ws = gpu_weight(N, K, 3, cuda_device)
+    out = fp8gq.fused_gemv_quant(x, wq, ws, kernel="row")
+    _, exact, _, _ = oracle_of(x, wq, ws)
+    assert_close(to_f32(out), exact, 2.0)
+
+
+def test_row_kernel_strided_weight(fp8gq, cuda_device):
+    """Weight rows padded (ldw > K): the per-row bulk-copy path."""
+    K, N = 1024, 768
+    x = gpu_activation(1, K, 5, cuda_device)
+    wq, ws = gpu_weight(N, K, 6, cuda_device)
+    big = torch.zeros(N, K + 256, dtype=torch.float8_e4m3fn, device=cuda_device)
+    big[:, :K] = wq
+    out = fp8gq.fused_gemv_quant(x, big[:, :K], ws)
+    _, exact, _, _ = oracle_of(x, wq, ws)
+    assert_close(to_f32(out), exact, 2.0)
+
+
+def test_row_kernel_deterministic(fp8gq, cuda_device):
+    x = gpu_activation(1, 4096, 9, cuda_device)
+    wq, ws = gpu_weight(6144, 4096, 10, cuda_device)
+    a = fp8gq.fused_gemv_quant(x, wq, ws)
+    b = fp8gq.fused_gemv_quant(x, wq, ws)
+    assert torch.equal(a, b)
+
+
+# ----------------------------------------------------------- tile kernel --
+
+@pytest.mark.parametrize("M", [2, 4, 8, 16])
+@pytest.mark.parametrize("name", list(QWEN3_4B))
+def test_tile_kernel_qwen3_4b(fp8gq, cuda_device, M, name):
+    K, N = QWEN3_4B[name]
+    x = gpu_activation(M, K, 20 + M, cuda_device)
+    wq, ws = gpu_weight(N, K, 21, cuda_device)
+    out, xq, sx = fp8gq.fused_gemv_quant(x, wq, ws, return_quant=True)
+    _, exact, rq, rs = oracle_of(x, wq, ws)
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert_close(to_f32(out), exact, 3.0)
+
+
+@pytest.mark.parametrize("M", [1, 17, 33, 64, 65, 100])
+def test_tile_kernel_token_tiles(fp8gq, cuda_device, M):
+    K, N = 1024, 1280
+    x = gpu_activation(M, K, 30 + M, cuda_device)
+    wq, ws = gpu_weight(N, K, 31, cuda_device)
+    out = fp8gq.fused_gemv_quant(x, wq, ws, kernel="tm")
+    _, exact, _, _ = oracle_of(x, wq, ws)
+    assert_close(to_f32(out), exact, 3.0)
+
+
+@pytest.mark.parametrize("name", list(QWEN3_8B))
+def test_tile_kernel_m1_matches_row_kernel(fp8gq, cuda_device, name):
+    K, N = QWEN3_8B[name]
+    x = gpu_activation(1, K, 40, cuda_device)
+    wq, ws = gpu_weight(N, K, 41, cuda_device)
+    tm = fp8gq.fused_gemv_quant(x, wq, ws, kernel="tm")
+    _, exact, _, _ = oracle_of(x, wq, ws)
+    assert_close(to_f32(tm), exact, 3.0)
+
+
+def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
+    M, K, N = 6, 2048, 1536
+    xb = gpu_activation(M, K + 64, 50, cuda_device)
+    x = xb[:, :K]                                         # ldx = K + 64
+    wq, ws = gpu_weight(N, K, 51, cuda_device)
+    out_big = torch.full((M, N + 128), 3.0, dtype=torch.bfloat16, device=cuda_device)
+    fp8gq.fused_gemv_quant(x, wq, ws, out=out_big[:, :N])
+    a = out_big[:, :N].clone()
+    fp8gq.fused_gemv_quant(x, wq, ws, out=out_big[:, :N])
+    assert torch.equal(a, out_big[:, :N])                 # split-K fixup is deterministic
+    assert torch.all(out_big[:, N:] == 3.0)               # nothing written past ldo's row
+    _, exact, _, _ = oracle_of(x.contiguous(), wq, ws)
+    assert_close(to_f32(a), exact, 3.0)
+
+
+# ---------------------------------------------------------------- SwiGLU --
+
+@pytest.mark.parametrize("M", [1, 2, 16])
+def test_swiglu_down_proj(fp8gq, cuda_device, M):
+    I, N = 12288, 4096
+    gu = gpu_activation(M, 2 * I, 60 + M, cuda_device, std=1.5, outliers=False)
+    wq, ws = gpu_weight(N, I, 61, cuda_device)
+    out, xq, sx = fp8gq.fused_swiglu_q_gemm(gu, wq, ws, return_quant=True)
+    _, exact, rq, rs = oracle_of(gu, wq, ws, swiglu=True)
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert_close(to_f32(out), exact, 2.0 if M == 1 else 3.0)
+
+
+# ------------------------------------------------------- the patch layer --
+
+def test_patch_wrappers_on_gpu(fp8gq, cuda_device):
+    import types
+    import fp8gq.patch_fp8_fused_tail as P
+    calls = []
+    mod = types.ModuleType("fp8_utils")
+    mod.flashinfer_gemm_w8a8_block_fp8_linear_with_fallback = lambda *a: calls.append(a) or None
+    P.install(mod)
+    try:
+        K, N = 4096, 6144
+        wq, ws = gpu_weight(N, K, 70, cuda_device)
+        for M in (1, 4):
+            x = gpu_activation(M, K, 71, cuda_device).view(M, 1, K)
+            bias = torch.randn(N, device=cuda_device).bfloat16()
+            out = mod.flashinfer_gemm_w8a8_block_fp8_linear_with_fallback(
+                input=x, weight=wq, block_size=[128, 128], weight_scale=ws, input_scale=None, bias=bias)
+            assert out.shape == (M, 1, N)
+            want = fp8gq.fused_gemv_quant(x.view(M, K), wq, ws) + bias
+            assert torch.equal(out.view(M, N), want)
+        assert not calls
+        x = gpu_activation(32, K, 72, cuda_device)
+        mod.flashinfer_gemm_w8a8_block_fp8_linear_with_fallback(x, wq, [128, 128], ws, None, None)
+        assert len(calls) == 1
+    finally:
+        P.uninstall(mod)
+
+
+def test_misaligned_activation_raises(fp8gq, cuda_device):
+    wq, ws = gpu_weight(256, 256, 80, cuda_device)
+    x = torch.zeros(1, 264, dtype=torch.bfloat16, device=cuda_device)[:, 4:260]
+    with pytest.raises(fp8gq.Fp8gqError) as e:
+        fp8gq.fused_gemv_quant(x, wq, ws)
+    assert e.value.status == 3
+
+
+def test_no_device_error_recorded(fp8gq, cuda_device):
+    torch.cuda.synchronize()
+    assert fp8gq.device_error() == 0
