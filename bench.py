@@ -49,6 +49,11 @@ WORKLOAD = ("qwen3-8b-fp8 decode linear stack, M=1: 36 layers x {qkv 4096->6144,
             "bf16 activations with 1x128 group quant")
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
+# from the ncu capture summarised in profiles/ (single-GPU gate_up case)
+NCU_TRAFFIC_BYTES = {"row": 100_719_872 + 3_674_368}
+
+
 def alg_bytes(M: int, K: int, N: int) -> int:
     """N*K weight bytes + fp32 block scales + bf16 activation in + bf16 out."""
     return N * K + 4 * (N // 128) * (K // 128) + 2 * M * K + 2 * M * N
@@ -65,6 +70,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None,
+                    help="launch one kernel case --warmup + --steps times and exit (for ncu): "
+                         "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down")
     return ap.parse_args()
 
 
@@ -325,10 +333,31 @@ def run_ours(args):
         per[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
                      "bytes_per_call": b}
         del g1
+    per_tm = {}
+    for i, (name, K, N) in enumerate(SHAPES):
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            for lin in layers:
+                _, _, _, wq, ws, x, out, shard = lin[i]
+                fp8gq.fused_gemv_quant(x, wq, ws, out=out if world == 1 else shard, kernel="tm")
+        g1.replay()
+        torch.cuda.synchronize()
+        reps = 20
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(reps):
+            g1.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) * 1e3 / (reps * LAYERS)
+        b = alg_bytes(1, K, N // world)
+        per_tm[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
+        del g1
     peak, peak_kind = measured_peak()
     gu = per["gate_up"]
     roofline = {"bound": "hbm", "achieved": gu["gbs"], "peak": peak, "unit": "GB/s",
-                "frac": round(gu["gbs"] / peak, 4), "traffic": None,
+                "frac": round(gu["gbs"] / peak, 4),
+                "traffic": NCU_TRAFFIC_BYTES["row"] if world == 1 else None,
                 "kernel": "gemv_row_kernel<1,4,false> (gate_up 4096->24576%s)" % (
                     f", N/{world} rows per rank" if world > 1 else ""),
                 "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)"}
@@ -378,15 +407,52 @@ def run_ours(args):
                            "parallelism": f"N-sharded x{world} + NCCL all-gather per linear" if world > 1
                            else "single GPU", "timing": "CUDA graph of one step, CUDA events"},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
-                "per_linear": per, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "per_linear": per, "per_linear_tile_kernel_m1": per_tm, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
+def run_profile_case(args):
+    """One linear of the stack, launched back to back; no timing, no output
+    checks.  Used as the command under ncu."""
+    import torch
+    import fp8gq
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    fp8gq.load()
+    parts = args.profile_case.split(":")
+    shape, kernel, M = parts[0], "auto", 1
+    for p in parts[1:]:
+        if p.startswith("M="):
+            M = int(p[2:])
+        else:
+            kernel = p
+    dims = {n: (K, N) for n, K, N in SHAPES}
+    dims["swiglu_down"] = (12288, 4096)
+    K, N = dims[shape]
+    wq, ws = make_weight_gpu(N, K, seed=1, dev=dev)
+    g = torch.Generator(device=dev).manual_seed(2)
+    if shape == "swiglu_down":
+        x = (torch.randn(M, 2 * K, generator=g, device=dev) * 1.5).bfloat16()
+        fn = lambda: fp8gq.fused_swiglu_q_gemm(x, wq, ws)  # noqa: E731
+    else:
+        x = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        fn = lambda: fp8gq.fused_gemv_quant(x, wq, ws, kernel=kernel)  # noqa: E731
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    assert fp8gq.device_error() == 0
+    print(json.dumps({"profile_case": args.profile_case, "launches": args.warmup + args.steps,
+                      "bytes_per_launch": alg_bytes(M, K, N)}))
+
+
 def main():
     args = parse()
+    if args.profile_case:
+        run_profile_case(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

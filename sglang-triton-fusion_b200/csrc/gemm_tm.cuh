@@ -45,6 +45,11 @@ constexpr int kTmThreads = 320;
 constexpr int kTmNAcc = 4;          // TMEM accumulator buffers
 constexpr int kTmSxRing = 32;       // >= stages + accumulators + 1
 constexpr int kTmATileBytes = 128 * 128;
+// The workspace starts with one split-K counter per 128-row block, in a region
+// of fixed size so that the partial sums of one shape never land on the
+// counters of another shape that shares the workspace.
+constexpr int kTmMaxRowBlocks = 4096;                       // N <= 524288
+constexpr size_t kTmCounterBytes = static_cast<size_t>(kTmMaxRowBlocks) * 4;
 
 struct TmParams {
   const __nv_bfloat16* x;   // [M, ldx] (plain) or [M, ldx] with [gate | up] (SwiGLU)
@@ -57,7 +62,7 @@ struct TmParams {
   int N, K;
   int KB;                   // K / 128
   int64_t U;                // (N/128) * KB tiles
-  int* counters;            // [N/128], zero on entry and exit
+  int* counters;            // [kTmMaxRowBlocks], zero on entry and exit
   float* partials;          // [G][2][MT][128]
   uint8_t* xq_out;          // optional [M, K]
   float* sx_out;            // optional [M, K/128]
@@ -430,8 +435,7 @@ inline size_t tm_workspace_bytes_for(int M, int N, int K, int sm_count) {
   const int MT = tm_token_tile(M);
   const int64_t U = static_cast<int64_t>(N / kGroup) * (K / kGroup);
   const int G = tm_grid(U, sm_count);
-  const size_t counters = ((static_cast<size_t>(N / kGroup) * 4 + 255) / 256) * 256;
-  return counters + static_cast<size_t>(G) * 2 * MT * 128 * sizeof(float);
+  return kTmCounterBytes + static_cast<size_t>(G) * 2 * MT * 128 * sizeof(float);
 }
 
 inline size_t tm_workspace_bytes(int M, int N, int K) {
@@ -487,6 +491,7 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
                      float* sx_out, void* workspace, size_t workspace_bytes, int sm_count, int max_smem,
                      cudaStream_t stream) {
   const int MT = tm_token_tile(M);
+  if (N / kGroup > kTmMaxRowBlocks) return 8;  // FP8GQ_ERR_UNSUPPORTED
   const size_t need = tm_workspace_bytes_for(M, N, K, sm_count);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return 5;  // FP8GQ_ERR_WORKSPACE
@@ -501,9 +506,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   p.K = K;
   p.KB = K / kGroup;
   p.U = static_cast<int64_t>(N / kGroup) * p.KB;
-  const size_t counters = ((static_cast<size_t>(N / kGroup) * 4 + 255) / 256) * 256;
   p.counters = static_cast<int*>(workspace);
-  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+  p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTmCounterBytes);
   const int grid = tm_grid(p.U, sm_count);
   for (int m0 = 0; m0 < M; m0 += MT) {
     p.x = static_cast<const __nv_bfloat16*>(x) + static_cast<int64_t>(m0) * ldx;

@@ -210,6 +210,21 @@ def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
     assert_close(to_f32(a), exact, 3.0)
 
 
+def test_tile_kernel_workspace_shared_across_shapes(fp8gq, cuda_device):
+    """Small-N and large-N calls alternate on one workspace: the split-K
+    counters of one shape must not be overwritten by another's partial sums."""
+    cases = [(2, 1024, 1280), (4, 4096, 24576), (3, 2560, 4096), (1, 4096, 24576), (16, 1024, 512)]
+    ops = []
+    for i, (M, K, N) in enumerate(cases):
+        x = gpu_activation(M, K, 90 + i, cuda_device)
+        wq, ws = gpu_weight(N, K, 95 + i, cuda_device)
+        ops.append((x, wq, ws, oracle_of(x, wq, ws)[1]))
+    for _ in range(2):
+        for x, wq, ws, exact in ops:
+            out = fp8gq.fused_gemv_quant(x, wq, ws, kernel="tm")
+            assert_close(to_f32(out), exact, 3.0)
+
+
 # ---------------------------------------------------------------- SwiGLU --
 
 @pytest.mark.parametrize("M", [1, 2, 16])
