@@ -47,8 +47,10 @@ enum fp8gq_status {
     FP8GQ_ERR_DEVICE = 6,        /* current device is not compute capability 10.x   */
     FP8GQ_ERR_LAUNCH = 7,        /* the CUDA launch failed                          */
     FP8GQ_ERR_UNSUPPORTED = 8,   /* shape outside what the selected kernel handles  */
-    FP8GQ_ERR_DEVICE_TIMEOUT = 9 /* a kernel's bounded wait gave up (see
+    FP8GQ_ERR_DEVICE_TIMEOUT = 9, /* a kernel's bounded wait gave up (see
                                     fp8gq_device_error)                             */
+    FP8GQ_ERR_SCRATCH_LIMIT = 10 /* the shape needs more scratch than the fixed
+                                    device buffer of fp8gq_gemv_quant_tm_noalloc    */
 };
 
 typedef void *fp8gq_stream_t;
@@ -121,6 +123,36 @@ int fp8gq_swiglu_group_quant(const void *gu, int64_t ldgu, int M, int I,
  * a kernel sets when one of its bounded waits gives up.  Synchronous.  0 means
  * no error was recorded. */
 int fp8gq_device_error(uint32_t *code, int clear);
+
+/* fp8gq_gemv_quant_tm without a workspace argument.  No counterpart in the
+ * reference (its Triton kernels need no scratch).
+ *
+ * For callers that cannot allocate device memory at the point of the call:
+ * inference servers that reserve nearly all of HBM up front for weights and
+ * KV cache and hand it out from a pool they do not let kernels draw on,
+ * latency-critical decode loops that cannot afford cudaMalloc's implicit
+ * device synchronisation, and plain C/FFI callers that have no allocator of
+ * their own to size and zero a workspace with.
+ * The tile kernel's split-K scratch lives instead in one fixed device array
+ * of FP8GQ_NOALLOC_SCRATCH_BYTES (4 MiB) inside libfp8gq, which every GPU
+ * that loads the library keeps until the process exits.  That bounds the
+ * shapes: a call whose scratch (fp8gq_workspace_bytes for M >= 2) exceeds
+ * the array returns FP8GQ_ERR_SCRATCH_LIMIT; on a 148-SM B200 every M <= 16
+ * with N <= 524288 fits.
+ *
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture begins.  Every call clears the array's split-K counters with an
+ * asynchronous memset on `stream` and then reuses the array, which keeps the
+ * last call's partial sums: calls whose kernels overlap on the GPU (two
+ * streams, two host threads) race on it, so issue them on one stream.
+ * Allocates nothing: no cudaMalloc, no cudaFree, no allocating library call.
+ */
+#define FP8GQ_NOALLOC_SCRATCH_BYTES (4u << 20)
+int fp8gq_gemv_quant_tm_noalloc(const void *x, int64_t ldx, const void *w, int64_t ldw,
+                                const float *ws, int64_t ldws, void *out, int64_t ldo,
+                                int M, int N, int K, uint8_t *xq_out, float *sx_out,
+                                fp8gq_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -172,6 +172,8 @@ const char* fp8gq_status_string(int status) {
     case FP8GQ_ERR_LAUNCH: return "CUDA kernel launch failed";
     case FP8GQ_ERR_UNSUPPORTED: return "shape not supported by the selected kernel";
     case FP8GQ_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait gave up (fp8gq_device_error has the site)";
+    case FP8GQ_ERR_SCRATCH_LIMIT:
+      return "shape needs more split-K scratch than the 4 MiB device buffer of fp8gq_gemv_quant_tm_noalloc";
     default: return "unknown fp8gq status";
   }
 }
@@ -272,3 +274,59 @@ int fp8gq_device_error(uint32_t* code, int clear) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// fp8gq_gemv_quant_tm_noalloc: the tile kernel with its split-K scratch in a
+// fixed device array instead of a caller-provided workspace, for callers that
+// cannot allocate (see include/fp8gq.h).  Nothing here allocates.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = FP8GQ_NOALLOC_SCRATCH_BYTES;
+
+// Zero-initialised when the library's module loads on a device; holds the
+// split-K counters (first kTmCounterBytes) and the partial sums.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address is looked up
+// once per device with that device current, and cached.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FP8GQ_ERR_DEVICE;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return FP8GQ_ERR_LAUNCH;
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return FP8GQ_OK;
+}
+
+}  // namespace
+
+extern "C" int fp8gq_gemv_quant_tm_noalloc(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                           const float* ws, int64_t ldws, void* out, int64_t ldo,
+                                           int M, int N, int K, uint8_t* xq_out, float* sx_out,
+                                           fp8gq_stream_t stream) {
+  int st = check_common(x, w, ws, out, M, N, K, ldw, ldws, ldo);
+  if (st != FP8GQ_OK) return st;
+  if (ldx < K || (ldx % 8) != 0) return ldx < K ? FP8GQ_ERR_STRIDE : FP8GQ_ERR_ALIGNMENT;
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  if (N / kGroup > kTmMaxRowBlocks || tm_workspace_bytes_for(M, N, K, di.sm_count) > kNoAllocScratchBytes)
+    return FP8GQ_ERR_SCRATCH_LIMIT;
+  void* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st != FP8GQ_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the split-K counters must start at zero
+  if (cudaMemsetAsync(scratch, 0, kTmCounterBytes, s) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, scratch,
+                   kNoAllocScratchBytes, di.sm_count, di.max_smem_optin, s);
+}

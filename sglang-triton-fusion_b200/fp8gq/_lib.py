@@ -24,6 +24,7 @@ STATUS = {
     7: "FP8GQ_ERR_LAUNCH",
     8: "FP8GQ_ERR_UNSUPPORTED",
     9: "FP8GQ_ERR_DEVICE_TIMEOUT",
+    10: "FP8GQ_ERR_SCRATCH_LIMIT",
 }
 
 # name -> (restype, argtypes); the order of include/fp8gq.h
@@ -42,6 +43,7 @@ SIGNATURES = {
     "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),
 }
 
 
