@@ -70,6 +70,9 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--static-weights", type=int, default=0,
+                    help="1: declare the weights static (fp8gq.set_static_weights), letting each "
+                         "kernel prefetch its first weight tiles before the previous one finishes")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down")
@@ -229,6 +232,7 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     fp8gq.load()
+    fp8gq.set_static_weights(bool(args.static_weights))
 
     def barrier():
         if world > 1:
@@ -405,7 +409,8 @@ def run_ours(args):
                            "bytes_per_step": STEP_BYTES,
                            "l2": "inputs larger than L2 (6.95 GB of weights per step, 126 MB L2)",
                            "parallelism": f"N-sharded x{world} + NCCL all-gather per linear" if world > 1
-                           else "single GPU", "timing": "CUDA graph of one step, CUDA events"},
+                           else "single GPU", "timing": "CUDA graph of one step, CUDA events",
+                           "static_weights": bool(args.static_weights)},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
                 "per_linear": per, "per_linear_tile_kernel_m1": per_tm, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks}

@@ -119,6 +119,18 @@ int fp8gq_group_quant(const void *x, int64_t ldx, int M, int K,
 int fp8gq_swiglu_group_quant(const void *gu, int64_t ldgu, int M, int I,
                              uint8_t *xq, float *sx, fp8gq_stream_t stream);
 
+/* Declares (enable != 0) that weights and their block scales are never written
+ * by work queued earlier on the stream of a call -- true in an inference server
+ * whose weights are loaded once.  The kernels are launched with programmatic
+ * dependent launch, so a call may start while the previous kernel on its
+ * stream is still running; with static weights it then already streams its
+ * first weight tiles and block scales before waiting for that kernel (the
+ * activation, output and workspace are never touched before the wait).  Off by
+ * default: leave it off when weights can change between calls (for example an
+ * online weight update followed directly by a call).  Process-wide; returns the
+ * previous setting.  No counterpart in the reference. */
+int fp8gq_set_static_weights(int enable);
+
 /* Reads (and with clear != 0 resets) the current device's error word, which
  * a kernel sets when one of its bounded waits gives up.  Synchronous.  0 means
  * no error was recorded. */
@@ -134,7 +146,7 @@ int fp8gq_device_error(uint32_t *code, int clear);
  * device synchronisation, and plain C/FFI callers that have no allocator of
  * their own to size and zero a workspace with.
  * The tile kernel's split-K scratch lives instead in one fixed device array
- * of FP8GQ_NOALLOC_SCRATCH_BYTES (4 MiB) inside libfp8gq, which every GPU
+ * of FP8GQ_NOALLOC_SCRATCH_BYTES (8 MiB) inside libfp8gq, which every GPU
  * that loads the library keeps until the process exits.  That bounds the
  * shapes: a call whose scratch (fp8gq_workspace_bytes for M >= 2) exceeds
  * the array returns FP8GQ_ERR_SCRATCH_LIMIT; on a 148-SM B200 every M <= 16
@@ -148,7 +160,7 @@ int fp8gq_device_error(uint32_t *code, int clear);
  * streams, two host threads) race on it, so issue them on one stream.
  * Allocates nothing: no cudaMalloc, no cudaFree, no allocating library call.
  */
-#define FP8GQ_NOALLOC_SCRATCH_BYTES (4u << 20)
+#define FP8GQ_NOALLOC_SCRATCH_BYTES (8u << 20)
 int fp8gq_gemv_quant_tm_noalloc(const void *x, int64_t ldx, const void *w, int64_t ldw,
                                 const float *ws, int64_t ldws, void *out, int64_t ldo,
                                 int M, int N, int K, uint8_t *xq_out, float *sx_out,

@@ -3,6 +3,7 @@
 // is the caller's workspace.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "../../include/fp8gq.h"
@@ -25,6 +26,7 @@ struct DeviceInfo {
 
 std::mutex g_mu;
 DeviceInfo g_dev[kMaxDevices];
+std::atomic<int> g_static_weights{0};
 
 int device_info(DeviceInfo* out, int* dev_out) {
   int dev = 0;
@@ -131,9 +133,10 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   p.stages = stages;
   p.xq_out = xq_out;
   p.sx_out = sx_out;
+  p.early_weights = g_static_weights.load(std::memory_order_relaxed);
   int grid = 2 * di.sm_count;
   if (grid > p.n_groups) grid = p.n_groups;
-  fn<<<grid, T + 32, smem, stream>>>(p);
+  if (launch_with_pdl(fn, dim3(grid), dim3(T + 32), smem, stream, p) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
   return launch_status();
 }
 
@@ -173,7 +176,7 @@ const char* fp8gq_status_string(int status) {
     case FP8GQ_ERR_UNSUPPORTED: return "shape not supported by the selected kernel";
     case FP8GQ_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait gave up (fp8gq_device_error has the site)";
     case FP8GQ_ERR_SCRATCH_LIMIT:
-      return "shape needs more split-K scratch than the 4 MiB device buffer of fp8gq_gemv_quant_tm_noalloc";
+      return "shape needs more split-K scratch than the 8 MiB device buffer of fp8gq_gemv_quant_tm_noalloc";
     default: return "unknown fp8gq status";
   }
 }
@@ -204,7 +207,8 @@ int fp8gq_gemv_quant_tm(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   st = device_info(&di, nullptr);
   if (st != FP8GQ_OK) return st;
   return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace,
-                   workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream));
+                   workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream),
+                   g_static_weights.load(std::memory_order_relaxed));
 }
 
 int fp8gq_fused_gemv_quant(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
@@ -236,7 +240,8 @@ int fp8gq_fused_swiglu_q_gemm(const void* gu, int64_t ldgu, const void* w, int64
   st = device_info(&di, nullptr);
   if (st != FP8GQ_OK) return st;
   return launch_tm(true, gu, ldgu, w, ldw, ws, ldws, out, ldo, M, N, I, xq_out, sx_out, workspace,
-                   workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream));
+                   workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream),
+                   g_static_weights.load(std::memory_order_relaxed));
 }
 
 int fp8gq_group_quant(const void* x, int64_t ldx, int M, int K, uint8_t* xq, float* sx,
@@ -259,6 +264,10 @@ int fp8gq_swiglu_group_quant(const void* gu, int64_t ldgu, int M, int I, uint8_t
       (reinterpret_cast<uintptr_t>(sx) & 3u))
     return FP8GQ_ERR_ALIGNMENT;
   return launch_quant(true, gu, ldgu, M, I, xq, sx, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_set_static_weights(int enable) {
+  return g_static_weights.exchange(enable ? 1 : 0);
 }
 
 int fp8gq_device_error(uint32_t* code, int clear) {
@@ -328,5 +337,6 @@ extern "C" int fp8gq_gemv_quant_tm_noalloc(const void* x, int64_t ldx, const voi
   // the split-K counters must start at zero
   if (cudaMemsetAsync(scratch, 0, kTmCounterBytes, s) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
   return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, scratch,
-                   kNoAllocScratchBytes, di.sm_count, di.max_smem_optin, s);
+                   kNoAllocScratchBytes, di.sm_count, di.max_smem_optin, s,
+                   g_static_weights.load(std::memory_order_relaxed));
 }

@@ -6,7 +6,10 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
+#include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <utility>
 
 namespace fp8gq {
 
@@ -101,6 +104,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   }
 }
 
+// mbar_wait by lane 0 only; the other lanes of the (converged) warp wait at
+// __syncwarp, which also orders what lane 0 observed before their accesses.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, unsigned int site, int lane) {
+  uint32_t ok = 1;
+  if (lane == 0) ok = mbar_wait(bar, parity, site) ? 1u : 0u;
+  __syncwarp();
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
 // global to this CTA's shared memory; completion is counted on `bar`.  The
 // weight stream is read once, so it is marked evict-first in L2.
@@ -118,6 +130,17 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
+
+// Programmatic dependent launch.  A kernel launched with
+// launch_with_pdl may start while the previous kernel in the stream is still
+// running; it does its set-up, then waits here before it touches anything the
+// previous kernel may write (activations, outputs, workspace).  Outside a
+// programmatic launch the wait is a no-op.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next programmatically launched kernel in the stream be scheduled
+// (it still waits for this grid to finish before reading our results).
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -190,6 +213,24 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   const float e = exp_cw(-g);
   const float s = __frcp_rn(__fadd_rn(1.0f, e));
   return __fmul_rn(__fmul_rn(g, s), u);
+}
+
+// Host: launch with programmatic stream serialization (the kernel pairs it with
+// grid_dependency_wait / grid_launch_dependents).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_with_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                   cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace fp8gq

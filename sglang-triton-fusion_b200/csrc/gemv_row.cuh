@@ -39,6 +39,7 @@ struct RowParams {
   int stages;               // ring depth
   uint8_t* xq_out;          // optional [K]
   float* sx_out;            // optional [K/128]
+  int early_weights;        // weights are static: fetch the first stages before the grid-dependency wait
 };
 
 constexpr int kRowMaxConsumerThreads = 384;  // the launcher never picks T > 384
@@ -154,11 +155,8 @@ gemv_row_kernel(const RowParams p) {
   if (warp == n_cwarps) {
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_first();
-      for (int j = 0; j < n_my; ++j) {
+      auto issue = [&](int j) {
         const int s = j % p.stages;
-        if (j >= p.stages) {
-          if (!mbar_wait(&empty[s], ((j / p.stages) & 1) ^ 1, kSiteRowEmpty)) break;
-        }
         mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(stage_bytes));
         const int64_t row0 = static_cast<int64_t>(g0 + j) * R;
         uint8_t* dst = smem + static_cast<size_t>(s) * stage_bytes;
@@ -169,10 +167,24 @@ gemv_row_kernel(const RowParams p) {
           for (int r = 0; r < R; ++r)
             bulk_g2s(dst + r * p.K, p.w + (row0 + r) * p.ldw, static_cast<uint32_t>(p.K), &full[s], pol);
         }
+      };
+      // static weights: fill the ring before the grid-dependency wait
+      const int n_pre = p.early_weights ? (n_my < p.stages ? n_my : p.stages) : 0;
+      for (int j = 0; j < n_pre; ++j) issue(j);
+      grid_dependency_wait();
+      for (int j = n_pre; j < n_my; ++j) {
+        const int s = j % p.stages;
+        if (j >= p.stages) {
+          if (!mbar_wait(&empty[s], ((j / p.stages) & 1) ^ 1, kSiteRowEmpty)) break;
+        }
+        issue(j);
       }
+      grid_launch_dependents();
     }
     return;
   }
+  // the activation and the output belong to the stream's previous work
+  grid_dependency_wait();
 
   // ------------------------------------------------- consumers: prologue --
   // Quantise this thread's chunks of the activation (whole 128-groups are

@@ -43,6 +43,7 @@ SIGNATURES = {
     "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "fp8gq_set_static_weights": (_I, [_I]),
     "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),
 }
 
@@ -93,6 +94,13 @@ def status_string(status: int) -> str:
 def check(status: int, what: str) -> None:
     if status != 0:
         raise Fp8gqError(status, what)
+
+
+def set_static_weights(enable: bool) -> bool:
+    """Declare that weights and block scales are never written by work queued
+    earlier on the calling stream (see fp8gq_set_static_weights in
+    include/fp8gq.h).  Returns the previous setting."""
+    return bool(load().fp8gq_set_static_weights(1 if enable else 0))
 
 
 def device_error(clear: bool = False) -> int:

@@ -238,6 +238,48 @@ def test_swiglu_down_proj(fp8gq, cuda_device, M):
     assert_close(to_f32(out), exact, 2.0 if M == 1 else 3.0)
 
 
+# ------------------------------------------ launch ordering (PDL) --------
+
+@pytest.mark.parametrize("static_weights", [False, True])
+@pytest.mark.parametrize("M, kernel", [(1, "row"), (1, "tm"), (4, "tm")])
+def test_chained_linears_see_their_producer(fp8gq, cuda_device, static_weights, M, kernel):
+    """out1 = lin1(x); out2 = lin2(out1) back to back on one stream, eager and
+    in a CUDA graph: the second kernel may start early (programmatic dependent
+    launch) but must read out1 only after the first has finished."""
+    K1, N1, N2 = 2048, 4096, 2560
+    x = gpu_activation(M, K1, 110, cuda_device)
+    w1, s1 = gpu_weight(N1, K1, 111, cuda_device)
+    w2, s2 = gpu_weight(N2, N1, 112, cuda_device)
+    ref1 = fp8gq.fused_gemv_quant(x, w1, s1, kernel=kernel)
+    torch.cuda.synchronize()
+    ref2 = fp8gq.fused_gemv_quant(ref1, w2, s2, kernel=kernel)
+    torch.cuda.synchronize()
+    prev = fp8gq.set_static_weights(static_weights)
+    try:
+        out1 = torch.empty_like(ref1)
+        out2 = torch.empty_like(ref2)
+        for _ in range(3):
+            out1.zero_()
+            out2.zero_()
+            fp8gq.fused_gemv_quant(x, w1, s1, out=out1, kernel=kernel)
+            fp8gq.fused_gemv_quant(out1, w2, s2, out=out2, kernel=kernel)
+        torch.cuda.synchronize()
+        assert torch.equal(out1, ref1) and torch.equal(out2, ref2)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fp8gq.fused_gemv_quant(x, w1, s1, out=out1, kernel=kernel)
+            fp8gq.fused_gemv_quant(out1, w2, s2, out=out2, kernel=kernel)
+        for _ in range(3):
+            out1.zero_()
+            out2.zero_()
+            g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out1, ref1) and torch.equal(out2, ref2)
+        del g
+    finally:
+        fp8gq.set_static_weights(prev)
+
+
 # ------------------------------------------------------- the patch layer --
 
 def test_patch_wrappers_on_gpu(fp8gq, cuda_device):

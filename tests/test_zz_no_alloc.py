@@ -4,7 +4,7 @@ This entry point serves callers that cannot allocate device memory when they
 call the library -- a server that has already handed nearly all HBM to its own
 pool, a decode loop that cannot pay for cudaMalloc's implicit synchronisation,
 a C caller with no allocator to make a zeroed workspace.  Instead of a
-caller-provided workspace it uses a fixed 4 MiB device array inside the
+caller-provided workspace it uses a fixed 8 MiB device array inside the
 library, so it must agree with the workspace entry point (fp8gq_gemv_quant_tm)
 on every shape that fits, call after call, while the array keeps whatever the
 previous call left in it; shapes that do not fit must be refused.
@@ -77,8 +77,8 @@ def test_noalloc_matches_workspace_entry_point_twice(lib, cuda_device, M, K, N):
 
 
 def test_noalloc_refuses_shapes_beyond_its_scratch(lib, cuda_device):
-    # M = 64 needs 64-token partial sums for every CTA: more than 4 MiB
+    # M = 64 needs 64-token partial sums for every CTA: more than 8 MiB
     x, wq, ws = _operands(64, 1024, 2048, seed=5, dev=cuda_device)
     out = torch.empty(64, 2048, dtype=torch.bfloat16, device=cuda_device)
     assert _call_noalloc(lib, x, wq, ws, out) == 10          # FP8GQ_ERR_SCRATCH_LIMIT
-    assert b"4 MiB" in lib.fp8gq_status_string(10)
+    assert b"8 MiB" in lib.fp8gq_status_string(10)
