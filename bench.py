@@ -16,9 +16,9 @@ value     algorithmic bytes per step / device time per step (CUDA graph of one
 e2e       the same metric through the public API (fp8gq.fused_gemv_quant,
           eager) with the step's activations copied in from pinned host
           memory and the outputs copied back, inside the timed region.
-roofline  the dominant kernel (gate_up, row kernel): algorithmic bytes per
-          launch / average launch duration (CUDA graph of 36 launches on
-          distinct weights), against MEASURED_PEAKS.json's hbm_gbs.
+roofline  the dominant kernel (gate_up; at M = 1 the tile kernel): algorithmic
+          bytes per launch / average launch duration (CUDA graph of 36 launches
+          on distinct weights), against MEASURED_PEAKS.json's hbm_gbs.
 cpu_baseline  the reference's PyTorch path (quantise, dequantise, fp32 matmul)
           on the host cores, on a bounded sample (rank 0, N = 1 only).
 
@@ -50,8 +50,19 @@ WORKLOAD = ("qwen3-8b-fp8 decode linear stack, M=1: 36 layers x {qkv 4096->6144,
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
-# from the ncu capture summarised in profiles/ (single-GPU gate_up case)
-NCU_TRAFFIC_BYTES = {"row": 100_719_872 + 3_674_368}
+# from the ncu captures summarised in profiles/ (single-GPU gate_up case)
+NCU_TRAFFIC_BYTES = {"gemv_row_kernel<false>": 100_719_872 + 3_674_368}
+
+# M == 1 routing of fp8gq_fused_gemv_quant / fp8gq_fused_swiglu_q_gemm: the row
+# kernel for weights of at most 20 MiB (and K <= 49152), the tile kernel above.
+ROW_PREFER_BYTES = 20 << 20
+
+
+def ROUTED_KERNEL(N: int, K: int, swiglu: bool = False) -> str:
+    sw = "true" if swiglu else "false"
+    if N * K <= ROW_PREFER_BYTES and K <= 49152:
+        return f"gemv_row_kernel<{sw}>"
+    return f"gemm_tm_kernel<16,{sw}>"
 
 
 def alg_bytes(M: int, K: int, N: int) -> int:
@@ -75,7 +86,8 @@ def parse():
                          "kernel prefetch its first weight tiles before the previous one finishes")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
-                         "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down")
+                         "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
+                         "or 'stack' for the whole decode step's routed linears")
     return ap.parse_args()
 
 
@@ -316,54 +328,75 @@ def run_ours(args):
     launches = LAYERS * len(SHAPES) * args.steps
 
     # ---- per-linear device time: graph of the 36 launches of one shape
-    per = {}
-    for i, (name, K, N) in enumerate(SHAPES):
+    def graph_us(calls, reps=20):
         g1 = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g1):
-            for lin in layers:
-                _, _, _, wq, ws, x, out, shard = lin[i]
-                fp8gq.fused_gemv_quant(x, wq, ws, out=out if world == 1 else shard)
+            for c in calls:
+                c()
         g1.replay()
         torch.cuda.synchronize()
-        reps = 20
         s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s0.record()
         for _ in range(reps):
             g1.replay()
         s1.record()
         torch.cuda.synchronize()
-        us = s0.elapsed_time(s1) * 1e3 / (reps * LAYERS)
-        b = alg_bytes(1, K, N // world)
-        per[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
-                     "bytes_per_call": b}
         del g1
-    per_tm = {}
-    for i, (name, K, N) in enumerate(SHAPES):
-        g1 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g1):
+        return s0.elapsed_time(s1) * 1e3 / (reps * len(calls))
+
+    def per_shape(kernel):
+        res = {}
+        for i, (name, K, N) in enumerate(SHAPES):
+            calls = []
             for lin in layers:
                 _, _, _, wq, ws, x, out, shard = lin[i]
-                fp8gq.fused_gemv_quant(x, wq, ws, out=out if world == 1 else shard, kernel="tm")
-        g1.replay()
-        torch.cuda.synchronize()
-        reps = 20
-        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s0.record()
-        for _ in range(reps):
-            g1.replay()
-        s1.record()
-        torch.cuda.synchronize()
-        us = s0.elapsed_time(s1) * 1e3 / (reps * LAYERS)
-        b = alg_bytes(1, K, N // world)
-        per_tm[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
-        del g1
+                o = out if world == 1 else shard
+                calls.append(lambda x=x, wq=wq, ws=ws, o=o: fp8gq.fused_gemv_quant(x, wq, ws, out=o, kernel=kernel))
+            us = graph_us(calls)
+            b = alg_bytes(1, K, N // world)
+            res[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1), "bytes_per_call": b}
+            if kernel == "auto":
+                res[name]["kernel"] = ROUTED_KERNEL(N // world, K)
+        return res
+
+    per = per_shape("auto")
+    per_row = per_shape("row")
+    per_tm = per_shape("tm")
+
+    extra = {}
+    if world == 1:
+        # fused SwiGLU + quant + down_proj at M = 1 (gate_up output 24576 -> 4096)
+        gus = [(torch.randn(1, 24576, device=dev) * 1.5).bfloat16() for _ in range(4)]
+        calls = [lambda lin=lin, gu=gus[i % 4]: fp8gq.fused_swiglu_q_gemm(gu, lin[3][3], lin[3][4], out=lin[3][6])
+                 for i, lin in enumerate(layers)]
+        us = graph_us(calls)
+        b = alg_bytes(1, 12288, 4096) + 2 * 12288
+        extra["swiglu_down_m1"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                                   "kernel": ROUTED_KERNEL(4096, 12288, swiglu=True)}
+        # TM-blocked small batches on the Qwen3-4B shapes (weights rotate through
+        # more than 4x the L2 so every call streams from HBM)
+        tmb = {}
+        for name, K, N in (("q", 2560, 4096), ("gate_up", 2560, 19456), ("down", 9728, 2560)):
+            copies = max(4, -(-4 * 126 * 2**20 // (N * K)))
+            wl = [make_weight_gpu(N, K, seed=500 + c, dev=dev) for c in range(copies)]
+            for M in (2, 4, 8, 16):
+                xm = torch.randn(M, K, device=dev).bfloat16()
+                om = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+                calls = [lambda w=w: fp8gq.fused_gemv_quant(xm, w[0], w[1], out=om) for w in wl]
+                us = graph_us(calls, reps=max(4, 200 // copies))
+                b = alg_bytes(M, K, N)
+                tmb[f"{name}_M{M}"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
+            del wl
+        extra["tm_blocked_qwen3_4b"] = tmb
+        torch.cuda.empty_cache()
+
     peak, peak_kind = measured_peak()
     gu = per["gate_up"]
     roofline = {"bound": "hbm", "achieved": gu["gbs"], "peak": peak, "unit": "GB/s",
                 "frac": round(gu["gbs"] / peak, 4),
-                "traffic": NCU_TRAFFIC_BYTES["row"] if world == 1 else None,
-                "kernel": "gemv_row_kernel<1,4,false> (gate_up 4096->24576%s)" % (
-                    f", N/{world} rows per rank" if world > 1 else ""),
+                "traffic": NCU_TRAFFIC_BYTES.get(gu["kernel"]) if world == 1 else None,
+                "kernel": "%s (gate_up 4096->24576%s)" % (
+                    gu["kernel"], f", N/{world} rows per rank" if world > 1 else ""),
                 "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)"}
 
     # ---- e2e: public API, eager, host buffers in and out
@@ -412,7 +445,8 @@ def run_ours(args):
                            else "single GPU", "timing": "CUDA graph of one step, CUDA events",
                            "static_weights": bool(args.static_weights)},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
-                "per_linear": per, "per_linear_tile_kernel_m1": per_tm, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "per_linear": per, "per_linear_row_kernel": per_row, "per_linear_tile_kernel": per_tm, **extra,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
                 "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -427,6 +461,22 @@ def run_profile_case(args):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
     fp8gq.load()
+    if args.profile_case == "stack":
+        # the decode step's 144 routed linears (36 layers x 4 shapes), eager
+        lin = []
+        g = torch.Generator(device=dev).manual_seed(2)
+        for L in range(LAYERS):
+            for i, (name, K, N) in enumerate(SHAPES):
+                wq, ws = make_weight_gpu(N, K, seed=100000 * L + 1000 * i, dev=dev)
+                lin.append((torch.randn(1, K, generator=g, device=dev).bfloat16(), wq, ws))
+        for _ in range(args.warmup + args.steps):
+            for x, wq, ws in lin:
+                fp8gq.fused_gemv_quant(x, wq, ws)
+        torch.cuda.synchronize()
+        assert fp8gq.device_error() == 0
+        print(json.dumps({"profile_case": "stack", "launches": (args.warmup + args.steps) * len(lin),
+                          "bytes_per_step": STEP_BYTES}))
+        return
     parts = args.profile_case.split(":")
     shape, kernel, M = parts[0], "auto", 1
     for p in parts[1:]:

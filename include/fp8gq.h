@@ -61,10 +61,13 @@ int fp8gq_version(void);
 /* Static, human-readable text for a status code. */
 const char *fp8gq_status_string(int status);
 
-/* Fused quant + GEMV, routed by M exactly like the reference wrapper
- * fused_gemv_quant (kernels/fused_gemv_quant_tm.py:83-102): M == 1 runs the
- * row kernel (fp8gq_gemv_quant_row), M > 1 the tensor-core tile kernel
- * (fp8gq_gemv_quant_tm).  `workspace` must hold fp8gq_workspace_bytes(M, N, K)
+/* Fused quant + GEMV, routed by M like the reference wrapper
+ * fused_gemv_quant (kernels/fused_gemv_quant_tm.py:83-102): M > 1 runs the
+ * tensor-core tile kernel (fp8gq_gemv_quant_tm); M == 1 runs the row kernel
+ * (fp8gq_gemv_quant_row) when the weight is at most 20 MiB (N * K bytes) and
+ * K <= 49152, and the tile kernel otherwise (on B200 it streams large weights
+ * faster).  Both produce the same quantised bytes; outputs agree within the
+ * accumulation-order tolerance.  `workspace` must hold fp8gq_workspace_bytes(M, N, K)
  * bytes (it may be NULL when that is 0) and be zero-filled before its first
  * use; kernels leave it zero-filled again when they finish.  Calls that share
  * a workspace must not overlap on the GPU. */
@@ -74,7 +77,7 @@ int fp8gq_fused_gemv_quant(const void *x, int64_t ldx, const void *w, int64_t ld
                            void *workspace, size_t workspace_bytes, fp8gq_stream_t stream);
 
 /* Scratch bytes fp8gq_fused_gemv_quant / fp8gq_fused_swiglu_q_gemm need for
- * this shape (0 when the routed kernel needs none).  K is the contraction
+ * this shape (0 when the routed kernel -- the row kernel -- needs none).  K is the contraction
  * length (I for the SwiGLU entry point). */
 size_t fp8gq_workspace_bytes(int M, int N, int K);
 
@@ -100,8 +103,9 @@ int fp8gq_gemv_quant_tm(const void *x, int64_t ldx, const void *w, int64_t ldw,
  *   act = silu(gu[:, :I]) * gu[:, I:]   (fp32),   out = GEMV(quant(act), w)
  * gu bf16 [M, 2I] row stride ldgu, w e4m3 [N, I], ws [N/128, I/128].
  * Replaces fused_swiglu_q_gemm / swiglu_q_gemm_kernel
- * (kernels/fused_swiglu_quant_gemv.py:26-67).  xq_out / sx_out as above,
- * with K = I. */
+ * (kernels/fused_swiglu_quant_gemv.py:26-67).  Routed like
+ * fp8gq_fused_gemv_quant (M == 1 and N * I <= 20 MiB: row kernel).  xq_out /
+ * sx_out as above, with K = I. */
 int fp8gq_fused_swiglu_q_gemm(const void *gu, int64_t ldgu, const void *w, int64_t ldw,
                               const float *ws, int64_t ldws, void *out, int64_t ldo,
                               int M, int N, int I, uint8_t *xq_out, float *sx_out,
@@ -130,6 +134,23 @@ int fp8gq_swiglu_group_quant(const void *gu, int64_t ldgu, int M, int I,
  * online weight update followed directly by a call).  Process-wide; returns the
  * previous setting.  No counterpart in the reference. */
 int fp8gq_set_static_weights(int enable);
+
+/* Tile-kernel strategy switches (fp8gq_gemv_quant_tm and the M > 1 paths),
+ * a bit mask; 0 (the default) picks each strategy where it fits:
+ *   FP8GQ_TM_STREAM_ACTIVATIONS  never use the resident activation feed (a CTA
+ *       quantising the activation of its whole K range into shared memory once,
+ *       before its weight stream starts); every K block's activation tile then
+ *       travels with its weight tile and is quantised on arrival;
+ *   FP8GQ_TM_WORKSPACE_SPLITK   never reduce split-K partial sums inside a
+ *       thread-block cluster (over distributed shared memory); they go through
+ *       the workspace and the last CTA of the row block adds them.
+ * Every combination gives bit-identical results (same products, same order of
+ * additions); the switches exist for testing and measurement.  Process-wide;
+ * returns the previous mask, or -1 for unknown bits.  No counterpart in the
+ * reference. */
+#define FP8GQ_TM_STREAM_ACTIVATIONS 1
+#define FP8GQ_TM_WORKSPACE_SPLITK 2
+int fp8gq_set_tm_options(int flags);
 
 /* Reads (and with clear != 0 resets) the current device's error word, which
  * a kernel sets when one of its bounded waits gives up.  Synchronous.  0 means

@@ -27,6 +27,10 @@ struct DeviceInfo {
 std::mutex g_mu;
 DeviceInfo g_dev[kMaxDevices];
 std::atomic<int> g_static_weights{0};
+std::atomic<int> g_tm_options{0};   // FP8GQ_TM_* bits
+
+int tm_resident_mode() { return (g_tm_options.load(std::memory_order_relaxed) & FP8GQ_TM_STREAM_ACTIVATIONS) ? 0 : 1; }
+int tm_cluster_mode() { return (g_tm_options.load(std::memory_order_relaxed) & FP8GQ_TM_WORKSPACE_SPLITK) ? 0 : 1; }
 
 int device_info(DeviceInfo* out, int* dev_out) {
   int dev = 0;
@@ -90,6 +94,13 @@ RowKernel row_lookup(int ci, int ri) {
 }
 
 constexpr int kRowMaxK = 8 * 384 * 16;      // C = 8 chunks of 16 per thread, T <= 384
+// M == 1 routing: the row kernel (CUDA cores, no split-K) wins on small
+// weights, where the tile kernel's fixed prologue and split-K hand-off cost
+// more than they save; the tile kernel wins above this many weight bytes
+// (measured on B200 with the Qwen3-8B decode shapes: 16.8 MB row, 25.2 MB tile).
+constexpr int64_t kRowPreferBytes = 20ll << 20;
+
+bool m1_uses_row(int N, int K) { return K <= kRowMaxK && static_cast<int64_t>(N) * K <= kRowPreferBytes; }
 constexpr int kRowRingBytes = 96 * 1024;    // per CTA; two CTAs per SM
 
 int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const float* ws, int64_t ldws,
@@ -192,7 +203,7 @@ int fp8gq_gemv_quant_row(const void* x, const void* w, int64_t ldw, const float*
 
 size_t fp8gq_workspace_bytes(int M, int N, int K) {
   if (M < 1 || N <= 0 || K <= 0 || N % kGroup || K % kGroup) return 0;
-  if (M == 1 && K <= kRowMaxK) return 0;
+  if (M == 1 && m1_uses_row(N, K)) return 0;
   return tm_workspace_bytes(M, N, K);
 }
 
@@ -208,14 +219,15 @@ int fp8gq_gemv_quant_tm(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   if (st != FP8GQ_OK) return st;
   return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace,
                    workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream),
-                   g_static_weights.load(std::memory_order_relaxed));
+                   g_static_weights.load(std::memory_order_relaxed), 0, tm_resident_mode(),
+                   tm_cluster_mode());
 }
 
 int fp8gq_fused_gemv_quant(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
                            int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
                            float* sx_out, void* workspace, size_t workspace_bytes,
                            fp8gq_stream_t stream) {
-  if (M == 1 && K <= kRowMaxK) {
+  if (M == 1 && m1_uses_row(N, K)) {
     int st = check_common(x, w, ws, out, M, N, K, ldw, ldws, ldo);
     if (st != FP8GQ_OK) return st;
     return launch_row(false, x, w, ldw, ws, ldws, out, N, K, xq_out, sx_out,
@@ -233,7 +245,7 @@ int fp8gq_fused_swiglu_q_gemm(const void* gu, int64_t ldgu, const void* w, int64
   if (st != FP8GQ_OK) return st;
   if (ldgu < 2 * static_cast<int64_t>(I)) return FP8GQ_ERR_STRIDE;
   if (ldgu % 8) return FP8GQ_ERR_ALIGNMENT;
-  if (M == 1 && I <= kRowMaxK)
+  if (M == 1 && m1_uses_row(N, I))
     return launch_row(true, gu, w, ldw, ws, ldws, out, N, I, xq_out, sx_out,
                       static_cast<cudaStream_t>(stream));
   DeviceInfo di;
@@ -241,7 +253,8 @@ int fp8gq_fused_swiglu_q_gemm(const void* gu, int64_t ldgu, const void* w, int64
   if (st != FP8GQ_OK) return st;
   return launch_tm(true, gu, ldgu, w, ldw, ws, ldws, out, ldo, M, N, I, xq_out, sx_out, workspace,
                    workspace_bytes, di.sm_count, di.max_smem_optin, static_cast<cudaStream_t>(stream),
-                   g_static_weights.load(std::memory_order_relaxed));
+                   g_static_weights.load(std::memory_order_relaxed), 0, tm_resident_mode(),
+                   tm_cluster_mode());
 }
 
 int fp8gq_group_quant(const void* x, int64_t ldx, int M, int K, uint8_t* xq, float* sx,
@@ -268,6 +281,11 @@ int fp8gq_swiglu_group_quant(const void* gu, int64_t ldgu, int M, int I, uint8_t
 
 int fp8gq_set_static_weights(int enable) {
   return g_static_weights.exchange(enable ? 1 : 0);
+}
+
+int fp8gq_set_tm_options(int flags) {
+  if (flags & ~(FP8GQ_TM_STREAM_ACTIVATIONS | FP8GQ_TM_WORKSPACE_SPLITK)) return -1;
+  return g_tm_options.exchange(flags);
 }
 
 int fp8gq_device_error(uint32_t* code, int clear) {
@@ -338,5 +356,6 @@ extern "C" int fp8gq_gemv_quant_tm_noalloc(const void* x, int64_t ldx, const voi
   if (cudaMemsetAsync(scratch, 0, kTmCounterBytes, s) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
   return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, scratch,
                    kNoAllocScratchBytes, di.sm_count, di.max_smem_optin, s,
-                   g_static_weights.load(std::memory_order_relaxed));
+                   g_static_weights.load(std::memory_order_relaxed), 0, tm_resident_mode(),
+                   tm_cluster_mode());
 }

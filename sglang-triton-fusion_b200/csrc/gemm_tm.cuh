@@ -28,16 +28,27 @@
 // counter per row block) adds the partials in CTA order -- the result does not
 // depend on timing -- stores bf16 and re-zeroes the counter.
 //
-// Warp roles (320 threads, one CTA per SM):
-//   warp 0      TMA producer: the 128x128-byte weight tile (SWIZZLE_128B) and
-//               the bf16 activation tile(s) of the K block (no multicast).
+// Activation modes.  Streaming: each stage also carries the bf16 activation
+// tile of its K block (TMA), which an activation warp quantises into the B
+// tile once it lands.  Resident (the host picks it when the CTA's M x K-range
+// bytes fit in the ring's activation space, e.g. every M = 1 decode shape):
+// after the grid-dependency wait the CTA quantises its whole K range once
+// into shared memory, and an activation warp only copies the prebuilt bytes
+// into a stage's B tile as soon as the MMA has released that stage -- the B
+// tile is ready long before the weight tile lands, so only the weight stream
+// is on the critical path.
+//
+// Warp roles (320 threads):
+//   warp 0      TMA producer: the 128x128-byte weight tile (SWIZZLE_128B) and,
+//               streaming, the bf16 activation tile(s) of the K block (no
+//               multicast).  Starts right after the grid-dependency wait.
 //   warp 1      TMEM allocator and MMA issuer (one elected lane).
 //   warps 2-5   activation producers: with P of them active (P divides the
-//               ring depth), warp w takes the CTA's K blocks j = w-2 mod P,
-//               quantises x (or silu(g)*u) from shared memory into the
-//               swizzled B tile and publishes sx; P K blocks are quantised
-//               at once.
+//               ring depth), warp w takes the CTA's K blocks j = w-2 mod P and
+//               fills their B tiles (and, streaming, publishes sx).
 //   warps 6-9   epilogue: TMEM -> registers, scale, accumulate, store.
+//   Warps 2-9 also load the CTA's block scales and, resident, quantise the
+//   activation in the prologue.
 #pragma once
 
 #include <cuda.h>
@@ -63,9 +74,13 @@ constexpr size_t kTmCounterBytes = static_cast<size_t>(kTmMaxRowBlocks) * 4;
 constexpr size_t kTmSmemBudgetSm = 228 * 1024;   // shared memory per SM
 constexpr size_t kTmSmemReservedPerCta = 1024;   // what the runtime keeps per resident CTA
 
-// CTAs per SM: the 16-token tile runs two per SM (two MMA issue streams and
-// two pipelines per SM; its registers and TMEM columns allow it), the wider
-// token tiles one.
+constexpr int kTmMaxStages = 8;     // ring depth limit (barrier arrays are sized for it)
+constexpr int kTmMaxCluster = 8;    // largest split-K cluster (portable cluster size)
+
+// CTAs per SM the 16-token tile may run at (two MMA issue streams and two
+// pipelines per SM; its registers and TMEM columns allow it); the wider token
+// tiles run one.  A grid of at most one CTA per SM gets the whole SM's shared
+// memory instead, for a deeper ring.
 template <int MT>
 constexpr int tm_ctas_per_sm() { return MT == 16 ? 2 : 1; }
 constexpr int kTmWsCache = 512;     // block scales of the CTA's tiles kept in shared memory
@@ -80,11 +95,17 @@ struct TmParams {
   int lg_sw;                // log2(sw)
   int kpb;                  // K blocks per accumulator group = MT / sw
   int nacc;                 // accumulator buffers in use (<= kTmMaxAcc)
-  int stages;               // ring depth
+  int stages;               // ring depth S (<= kTmMaxStages)
+  int npw;                  // activation warps in use (divides S)
+  uint32_t b_off, x_off, bar_off;   // shared-memory layout (bytes from the 1 KB-aligned base)
   int N, K;
   int KB;                   // K / 128
   int64_t U;                // (N/128) * KB tiles
   uint32_t x_tile_bytes;    // bytes of one activation box (M rows x 128 bf16)
+  const __nv_bfloat16* x;   // activation rows of this pass (resident mode reads them directly)
+  int64_t ldx;
+  int resident;             // resident activation mode
+  int csize;                // split-K cluster size (1: none; the CTAs of a row block form a cluster)
   int early_weights;        // weights and block scales are static: load them before the grid-dependency wait
   int* counters;            // [kTmMaxRowBlocks], zero on entry and exit
   float* partials;          // [G][2][MT][128]
@@ -92,36 +113,34 @@ struct TmParams {
   float* sx_out;            // optional [M, K/128]
 };
 
+// Shared memory, from the 1 KB-aligned base:
+//   A tiles [S][16 KB] | B tiles [S][MT x 128 B] | activation region (streaming:
+//   [S] bf16 tiles; resident: xq of the K range) | full[8] xfull[8] empty[8]
+//   acc_full[ACC] tmem_empty[ACC] sx_tag[SXR] (8 B each) drain | misc[4] |
+//   sx ring (resident: sx of the K range) | ws cache
+// In cluster mode the A-tile area holds the CTA's split-K partial sums once
+// its MMAs are done.
 template <int MT, bool kSwiglu>
 struct TmCfg {
-  static constexpr int kCtasPerSm = tm_ctas_per_sm<MT>();
-  static constexpr size_t kTmSmemBudget =
-      (kTmSmemBudgetSm / kCtasPerSm - kTmSmemReservedPerCta) < 227 * 1024
-          ? (kTmSmemBudgetSm / kCtasPerSm - kTmSmemReservedPerCta) : 227 * 1024;
   static constexpr int kBTileBytes = MT * 128;
   static constexpr int kXTileBytes = MT * 256 * (kSwiglu ? 2 : 1);   // room for MT rows
-  static constexpr int kStageBytes = kTmATileBytes + kBTileBytes + kXTileBytes;
   static constexpr int kTmemCols = (kTmMaxAcc * MT <= 32) ? 32 : (kTmMaxAcc * MT <= 64) ? 64
                                    : (kTmMaxAcc * MT <= 128) ? 128 : 256;
-  static constexpr int kNumBars = 3 * 8 /*full, xfull, empty*/ + 2 * kTmMaxAcc + kTmSxRing + 1;
-  static constexpr size_t kFixedBytes = kNumBars * 8 + 16 + kTmSxRing * MT * 4 + kTmWsCache * 4 + 1024;
-  static constexpr int kFit =
-      ((kTmSmemBudget - kFixedBytes) / kStageBytes) < 8 ? static_cast<int>((kTmSmemBudget - kFixedBytes) / kStageBytes)
-                                                        : 8;
-  // The activation warps take K blocks round robin; their number divides the
-  // ring depth, so every stage is only ever waited on by one of them, use
-  // after use, and a phase-parity wait can never see a stale phase.
-  static constexpr int kStages = kFit >= 4 ? (kFit / 4) * 4 : kFit;
-  static constexpr int kProducerWarps = kStages >= 4 ? 4 : kStages;
-  // ring | full[8] xfull[8] empty[8] acc_full[ACC] tmem_empty[ACC] sx_tag[SXR] (8 B each) drain | misc
-  //      | sx ring | ws cache
-  static constexpr size_t kBarOffset = static_cast<size_t>(kStages) * kStageBytes;
-  static constexpr size_t kMiscOffset = kBarOffset + kNumBars * 8;
-  static constexpr size_t kSxOffset = kMiscOffset + 16;
-  static constexpr size_t kWsOffset = kSxOffset + kTmSxRing * MT * 4;
-  static constexpr size_t kSmemBytes = kWsOffset + kTmWsCache * 4 + 1024;  // +1 KB alignment slack
-  static_assert(kStages >= 2, "stage ring does not fit in shared memory");
+  static constexpr int kNumBars = 3 * kTmMaxStages /*full, xfull, empty*/ + 2 * kTmMaxAcc + kTmSxRing + 1;
+  static constexpr size_t kTailBytes = kNumBars * 8 + 16 + kTmSxRing * MT * 4 + kTmWsCache * 4;
+  static constexpr size_t kAlignSlack = 1024;
+  static_assert(kBTileBytes % 1024 == 0, "SW128 tiles need 1 KB alignment");
+  static_assert(MT * 128 * 4 <= 2 * kTmATileBytes, "cluster partial sums must fit in two A tiles");
 };
+
+// Ring depth from the bytes left for it: 8, 6, 4, 3, 2 or 1 stages, so that
+// the activation warps (4, 3, 4, 3, 2, 1 of them) divide the depth -- each
+// stage is then only ever waited on by one of them, use after use, and a
+// phase-parity wait can never see a stale phase.
+inline int tm_pick_stages(int64_t fit) {
+  return fit >= 8 ? 8 : fit >= 6 ? 6 : fit >= 4 ? 4 : static_cast<int>(fit < 0 ? 0 : fit);
+}
+inline int tm_producer_warps(int S) { return S % 4 == 0 ? 4 : S % 3 == 0 ? 3 : S; }
 
 // ----------------------------------------------------------------- PTX --
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* tmap, int x, int y,
@@ -137,6 +156,35 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
   return pol;
+}
+
+// Fetch a tensor map (a __grid_constant__ kernel parameter) into the TMA
+// descriptor cache ahead of its first use.
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// Cluster-wide barrier: every thread of every CTA of the cluster arrives; the
+// release/acquire pair orders shared-memory writes before it with
+// distributed-shared-memory reads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void tc_fence_before() {
@@ -221,9 +269,9 @@ struct TileCursor {
   int nb, kb, pos;     // row block, K block, position in the accumulator group
   int s;               // stage of the ring
   uint32_t ph;         // parity of that stage's current use
-  __device__ __forceinline__ void init(int64_t u0, int KB) {
-    nb = static_cast<int>(u0 / KB);
-    kb = static_cast<int>(u0 - static_cast<int64_t>(nb) * KB);
+  __device__ __forceinline__ void init(int nb0, int kb0) {
+    nb = nb0;
+    kb = kb0;
     pos = 0;
     s = 0;
     ph = 0;
@@ -256,31 +304,107 @@ struct AccCursor {
   }
 };
 
+// 16 activation values of one lane from two 16-byte words of bf16 (and, for
+// SwiGLU, the two matching words of the up half): act = silu(g) * u.
+template <bool kSwiglu>
+__device__ __forceinline__ void act16(float (&v)[16], uint4 a, uint4 b, uint4 ua, uint4 ub) {
+  const uint32_t xw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  if constexpr (kSwiglu) {
+    const uint32_t uw[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[2 * e] = silu_mul(bf16_lo(xw[e]), bf16_lo(uw[e]));
+      v[2 * e + 1] = silu_mul(bf16_hi(xw[e]), bf16_hi(uw[e]));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      v[2 * e] = bf16_lo(xw[e]);
+      v[2 * e + 1] = bf16_hi(xw[e]);
+    }
+  }
+}
+
+// Group quant over a lane octet (8 lanes x 16 values = one 128-wide group):
+// octet amax by shuffles, then this lane's 16 e4m3 bytes and the group scale.
+// All 32 lanes call it together; `live` is uniform within an octet (a dead
+// octet holds zeros and returns zeros).
+__device__ __forceinline__ uint4 quant16_octet(const float (&v)[16], bool live, float& sx) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+  sx = 0.0f;
+  if (live) {
+    sx = group_scale(amax);
+    const float sinv = __frcp_rn(sx);
+    packed.x = quant_pair(v[0], v[1], sinv) | (static_cast<uint32_t>(quant_pair(v[2], v[3], sinv)) << 16);
+    packed.y = quant_pair(v[4], v[5], sinv) | (static_cast<uint32_t>(quant_pair(v[6], v[7], sinv)) << 16);
+    packed.z = quant_pair(v[8], v[9], sinv) | (static_cast<uint32_t>(quant_pair(v[10], v[11], sinv)) << 16);
+    packed.w = quant_pair(v[12], v[13], sinv) | (static_cast<uint32_t>(quant_pair(v[14], v[15], sinv)) << 16);
+  }
+  return packed;
+}
+
+// Reads every field of the parameter block once.  A parameter's first use in
+// a warp can stall it for several hundred cycles (constant-cache miss); doing
+// them all at kernel entry, before the grid-dependency wait, moves those
+// misses off the pipeline's critical path.
+__device__ __forceinline__ void tm_touch_params(const TmParams& p) {
+  uint64_t t = reinterpret_cast<uint64_t>(p.ws) ^ static_cast<uint64_t>(p.ldws) ^
+               reinterpret_cast<uint64_t>(p.out) ^ static_cast<uint64_t>(p.ldo) ^
+               reinterpret_cast<uint64_t>(p.x) ^ static_cast<uint64_t>(p.ldx) ^ static_cast<uint64_t>(p.U) ^
+               reinterpret_cast<uint64_t>(p.counters) ^ reinterpret_cast<uint64_t>(p.partials) ^
+               reinterpret_cast<uint64_t>(p.xq_out) ^ reinterpret_cast<uint64_t>(p.sx_out);
+  uint32_t u = static_cast<uint32_t>(p.M ^ p.sw ^ p.lg_sw ^ p.kpb ^ p.nacc ^ p.stages ^ p.npw ^ p.N ^ p.K ^ p.KB ^
+                                     p.resident ^ p.csize ^ p.early_weights) ^
+               p.b_off ^ p.x_off ^ p.bar_off ^ p.x_tile_bytes;
+  asm volatile("" ::"l"(t), "r"(u));
+}
+
+// Place of the CTA's tile j in its accumulator group (TileCursor::pos after j
+// steps from the CTA's first tile, K block kb0): groups restart at the CTA's
+// first tile and at every row-block boundary.
+__device__ __forceinline__ int tile_pos(int j, int kb0, int KB, int kpb) {
+  const int t = kb0 + j;
+  const int jstart = t < KB ? 0 : j - t % KB;
+  return (j - jstart) & (kpb - 1);
+}
+
 // ------------------------------------------------------------- kernel --
 template <int MT, bool kSwiglu>
 __global__ void __launch_bounds__(kTmThreads, tm_ctas_per_sm<MT>())
 gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                const TmParams p) {
   using Cfg = TmCfg<MT, kSwiglu>;
-  constexpr int S = Cfg::kStages;
+  const int S = p.stages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
-  uint64_t* xfull = full + 8;
-  uint64_t* empty = xfull + 8;
-  uint64_t* acc_full = empty + 8;
+  uint8_t* const a_tiles = smem;                       // [S][128 x 128 B] weight tiles
+  uint8_t* const b_tiles = smem + p.b_off;             // [S][MT x 128 B] quantised activation tiles
+  // streaming: [S] bf16 activation tiles; resident: xq of the K range, [slot][M][128 B]
+  uint8_t* const x_tiles = smem + p.x_off;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+  uint64_t* xfull = full + kTmMaxStages;
+  uint64_t* empty = xfull + kTmMaxStages;
+  uint64_t* acc_full = empty + kTmMaxStages;
   uint64_t* tmem_empty = acc_full + kTmMaxAcc;
   // sequence tags: sx_tag[j % ring] = j + 1 once K block j's scales are in the
   // sx ring (a plain shared-memory flag; the epilogue polls it)
   volatile uint32_t* sx_tag = reinterpret_cast<volatile uint32_t*>(tmem_empty + kTmMaxAcc);
   uint64_t* drain = tmem_empty + kTmMaxAcc + kTmSxRing;  // MMA completion on the error path
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + Cfg::kMiscOffset);  // [0] tmem base, [1] last flag
-  float* sx_ring = reinterpret_cast<float*>(smem + Cfg::kSxOffset);      // [kTmSxRing][MT]
-  float* ws_cache = reinterpret_cast<float*>(smem + Cfg::kWsOffset);     // [min(J, kTmWsCache)]
+  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag
+  // streaming: [kTmSxRing][MT] ring indexed by j; resident: [slot][M]
+  float* sx_ring = reinterpret_cast<float*>(misc + 4);
+  float* ws_cache = sx_ring + kTmSxRing * MT;          // [min(J, kTmWsCache)]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  tm_touch_params(p);
 
   const int64_t G = gridDim.x;
   const int64_t u0 = (static_cast<int64_t>(blockIdx.x) * p.U) / G;
@@ -288,22 +412,35 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   const int J = static_cast<int>(u1 - u0);
   const int kpb = p.kpb;
   const int nacc = p.nacc;
+  // Resident K range: a CTA whose tiles cover a whole row block's K range
+  // (J >= KB) keeps every K block, slot = kb; otherwise its J tiles have J
+  // distinct K blocks (kb0, kb0 + 1, ... mod KB), slot = j.
+  const bool resident = p.resident != 0;
+  const bool res_full = J >= p.KB;
+  const int nkb = res_full ? p.KB : J;
+  // the CTA's first tile (row block nb0, K block kb0): the only 64-bit
+  // divisions, done before the grid-dependency wait
+  const int nb0 = static_cast<int>(u0 / p.KB);
+  const int kb0 = static_cast<int>(u0 - static_cast<int64_t>(nb0) * p.KB);
 
-  if (tid == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1 + 1);    // TMA arrive_expect_tx + the activation warp of the K block
-      mbar_init(&xfull[s], 1);       // TMA arrive_expect_tx (activation tile)
-      mbar_init(&empty[s], 1);       // tcgen05.commit
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmap_w);
+      if (!resident) prefetch_tensormap(&tmap_x);
     }
-    for (int a = 0; a < kTmMaxAcc; ++a) {
-      mbar_init(&acc_full[a], 1);    // tcgen05.commit
-      mbar_init(&tmem_empty[a], 4);  // 4 epilogue warps
+    if (lane < S) {
+      mbar_init(&full[lane], 1 + 1);     // TMA arrive_expect_tx + the activation warp of the K block
+      mbar_init(&xfull[lane], 1);        // TMA arrive_expect_tx (activation tile)
+      mbar_init(&empty[lane], 1);        // tcgen05.commit
     }
-    for (int r = 0; r < kTmSxRing; ++r) sx_tag[r] = 0u;
-    mbar_init(drain, 1);
+    if (lane < kTmMaxAcc) {
+      mbar_init(&acc_full[lane], 1);     // tcgen05.commit
+      mbar_init(&tmem_empty[lane], 4);   // 4 epilogue warps
+    }
+    if (lane == 0) mbar_init(drain, 1);
+    for (int r = lane; r < kTmSxRing; r += 32) sx_tag[r] = 0u;
     fence_mbar_init();
-  }
-  if (warp == 1) {
+  } else if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&misc[0])),
                  "r"(Cfg::kTmemCols));
@@ -316,33 +453,115 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   bool ok = true;
 
   // Block scales of this CTA's tiles, ws_cache[j] = ws[nb(j), kb(j)] (the host
-  // launches only shapes with J <= kTmWsCache), and -- when the caller declared
-  // the weights static -- the weight tiles of the first ring of stages are
-  // fetched before the grid-dependency wait, overlapping the previous kernel's
-  // tail.  Activations, outputs and the workspace are touched only after it.
+  // launches only shapes with J <= kTmWsCache), loaded by warps 2-9; and --
+  // when the caller declared the weights static -- the weight tiles of the
+  // first ring of stages are fetched before the grid-dependency wait,
+  // overlapping the previous kernel's tail.  Activations, outputs and the
+  // workspace are touched only after it.
   const bool early = p.early_weights != 0;
   const int n_pre = early ? (J < S ? J : S) : 0;
+  auto ws_at = [&](int j) {
+    const int t = kb0 + j;
+    const int dn = t / p.KB;
+    return __ldg(p.ws + static_cast<int64_t>(nb0 + dn) * p.ldws + (t - dn * p.KB));
+  };
   auto load_ws_cache = [&]() {
-    for (int j = tid; j < J; j += kTmThreads) {
-      const int64_t u = u0 + j;
-      ws_cache[j] = __ldg(p.ws + (u / p.KB) * p.ldws + (u % p.KB));
-    }
+    for (int j = tid - 64; j < J; j += kTmThreads - 64) ws_cache[j] = ws_at(j);
   };
   if (early) {
-    load_ws_cache();
+    if (warp >= 2) load_ws_cache();
     if (tid == 0) {
       const uint64_t pol_w = l2_policy_evict_first();
       TileCursor c;
-      c.init(u0, p.KB);
+      c.init(nb0, kb0);
       for (int j = 0; j < n_pre; ++j, c.next(p.KB, kpb, S)) {
         mbar_arrive_expect_tx(&full[c.s], kTmATileBytes);
-        tma_load_2d(smem + c.s * Cfg::kStageBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[c.s], pol_w);
+        tma_load_2d(a_tiles + c.s * kTmATileBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[c.s], pol_w);
       }
     }
   }
   grid_dependency_wait();
-  if (!early) load_ws_cache();
-  __syncthreads();
+  // Warps 0 and 1 start their loops at once; warps 2-9 first finish the block
+  // scales and, resident, quantise the CTA's K range (8 warps x 4 lane octets,
+  // one 128-wide group per octet and pass), then meet at barrier 1.
+  if (warp >= 2) {
+    // the first block-scale load of each thread is issued before the
+    // activation loads, and stored after them: one round trip for both
+    const int jw = tid - 64;
+    float ws_first = 0.0f;
+    if (!early && jw < J) ws_first = ws_at(jw);
+    // resident: the first ring's B tiles are built here as well (zeros, then
+    // the live rows as they are quantised), so the first MMAs wait only for
+    // their weight tiles
+    const int nfirst = J < S ? J : S;
+    if (resident) {
+      for (int i = tid - 64; i < nfirst * (Cfg::kBTileBytes / 16); i += kTmThreads - 64)
+        reinterpret_cast<uint4*>(b_tiles)[i] = make_uint4(0u, 0u, 0u, 0u);
+      named_bar_sync(1, kTmThreads - 64);
+      const int oct = (warp - 2) * 4 + (lane >> 3);
+      const int chunk = lane & 7;
+      const int ngroups = p.M * nkb;
+      for (int g0 = 0; g0 < ngroups; g0 += 32) {
+        const int g = g0 + oct;
+        const bool live = g < ngroups;
+        const int m = live ? g / nkb : 0;
+        const int r = live ? g - m * nkb : 0;
+        int kb = res_full ? r : kb0 + r;
+        if (kb >= p.KB) kb -= p.KB;
+        float v[16];
+        if (live) {
+          // L2-coherent loads: the activation may come from the kernel before
+          // this one in the stream
+          const __nv_bfloat16* xr = p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 + chunk * 16;
+          const uint4 xa = __ldcg(reinterpret_cast<const uint4*>(xr));
+          const uint4 xb = __ldcg(reinterpret_cast<const uint4*>(xr) + 1);
+          uint4 ua = xa, ub = xb;
+          if constexpr (kSwiglu) {
+            ua = __ldcg(reinterpret_cast<const uint4*>(xr + p.K));
+            ub = __ldcg(reinterpret_cast<const uint4*>(xr + p.K) + 1);
+          }
+          act16<kSwiglu>(v, xa, xb, ua, ub);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+        }
+        float sx;
+        const uint4 packed = quant16_octet(v, live, sx);
+        if (live) {
+          *reinterpret_cast<uint4*>(x_tiles + (static_cast<int64_t>(r) * p.M + m) * 128 + chunk * 16) = packed;
+          if (chunk == 0) sx_ring[r * p.M + m] = sx;
+          // first-ring tiles j < nfirst that use slot r: j = r (slot = tile),
+          // or j = r - kb0 mod KB and every KB after it (slot = K block)
+          int jj = r;
+          int step = nfirst;
+          if (res_full) {
+            jj = r - kb0;
+            if (jj < 0) jj += p.KB;
+            step = p.KB;
+          }
+          for (; jj < nfirst; jj += step) {
+            const int br = tile_pos(jj, kb0, p.KB, kpb) * p.sw + m;
+            *reinterpret_cast<uint4*>(b_tiles + jj * Cfg::kBTileBytes + br * 128 + ((chunk ^ (br & 7)) << 4)) =
+                packed;
+          }
+          if (kb >= u0 && kb < u1) {
+            // this CTA holds tile (row block 0, kb): it writes the optional outputs
+            if (p.xq_out)
+              *reinterpret_cast<uint4*>(p.xq_out + static_cast<int64_t>(m) * p.K + kb * 128 + chunk * 16) = packed;
+            if (p.sx_out && chunk == 0) p.sx_out[static_cast<int64_t>(m) * p.KB + kb] = sx;
+          }
+        }
+      }
+    }
+    if (!early) {
+      if (jw < J) ws_cache[jw] = ws_first;
+      for (int j = jw + (kTmThreads - 64); j < J; j += kTmThreads - 64) ws_cache[j] = ws_at(j);
+    }
+    if (resident) fence_proxy_async_smem();   // B tiles written here are read by the MMA
+    named_bar_sync(1, kTmThreads - 64);
+    if (resident && tid == 64)
+      for (int j = 0; j < nfirst; ++j) mbar_arrive(&full[j]);
+  }
 
   if (warp == 0) {
     // --------------------------------------------------- TMA producer --
@@ -352,20 +571,21 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const uint32_t xbytes = p.x_tile_bytes * (kSwiglu ? 2u : 1u);
       int issued = 0;
       TileCursor c;
-      c.init(u0, p.KB);
+      c.init(nb0, kb0);
       for (int j = 0; j < J && ok; ++j, c.next(p.KB, kpb, S)) {
         const int s = c.s;
         if (j >= S) ok = mbar_wait(&empty[s], c.ph ^ 1u, kSiteTmA);
         if (!ok) break;
-        uint8_t* stage = smem + s * Cfg::kStageBytes;
-        uint8_t* xt = stage + kTmATileBytes + Cfg::kBTileBytes;
         if (j >= n_pre) {
           mbar_arrive_expect_tx(&full[s], kTmATileBytes);
-          tma_load_2d(stage, &tmap_w, c.kb * 128, c.nb * 128, &full[s], pol_w);
+          tma_load_2d(a_tiles + s * kTmATileBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[s], pol_w);
         }
-        mbar_arrive_expect_tx(&xfull[s], xbytes);
-        tma_load_2d(xt, &tmap_x, c.kb * 128, 0, &xfull[s], pol_x);
-        if constexpr (kSwiglu) tma_load_2d(xt + p.x_tile_bytes, &tmap_x, p.K + c.kb * 128, 0, &xfull[s], pol_x);
+        if (!resident) {
+          uint8_t* xt = x_tiles + s * static_cast<uint32_t>(Cfg::kXTileBytes);
+          mbar_arrive_expect_tx(&xfull[s], xbytes);
+          tma_load_2d(xt, &tmap_x, c.kb * 128, 0, &xfull[s], pol_x);
+          if constexpr (kSwiglu) tma_load_2d(xt + p.x_tile_bytes, &tmap_x, p.K + c.kb * 128, 0, &xfull[s], pol_x);
+        }
         issued = j + 1;
       }
       grid_launch_dependents();
@@ -373,7 +593,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         // let the copies already issued land before the CTA can exit
         for (int j = (issued > S ? issued - S : 0); j < issued; ++j) {
           mbar_wait(&full[j % S], (j / S) & 1, kSiteTmA);
-          mbar_wait(&xfull[j % S], (j / S) & 1, kSiteTmA);
+          if (!resident) mbar_wait(&xfull[j % S], (j / S) & 1, kSiteTmA);
         }
       }
     }
@@ -381,13 +601,14 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     // ----------------------------------------------------- MMA issuer --
     if (lane == 0) {
       const uint32_t idesc = idesc_f8<MT>();
-      // descriptors of stage 0's A tile; a stage, a K step and the B tile are
+      // descriptors of stage 0's A and B tiles; a stage and a K step are
       // offsets in the 14-bit start-address field (addresses < 256 KB)
-      const uint64_t desc0 = smem_desc_sw128(smem_u32(smem));
+      const uint64_t desc_a0 = smem_desc_sw128(smem_u32(a_tiles));
+      const uint64_t desc_b0 = smem_desc_sw128(smem_u32(b_tiles));
       AccCursor acc;
       uint32_t d_tmem = tmem_base;
       TileCursor c;
-      c.init(u0, p.KB);
+      c.init(nb0, kb0);
       for (int j = 0; j < J && ok; ++j, c.next(p.KB, kpb, S)) {
         if (c.pos == 0) {
           acc.start_group(nacc);
@@ -398,8 +619,8 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         ok = mbar_wait(&full[c.s], c.ph, kSiteTmB);
         if (!ok) break;
         tc_fence_after();
-        const uint64_t da = desc0 + static_cast<uint64_t>((c.s * Cfg::kStageBytes) >> 4);
-        const uint64_t db = da + (kTmATileBytes >> 4);
+        const uint64_t da = desc_a0 + static_cast<uint64_t>((c.s * kTmATileBytes) >> 4);
+        const uint64_t db = desc_b0 + static_cast<uint64_t>((c.s * Cfg::kBTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           mma_f8(d_tmem, da + 2 * kk, db + 2 * kk, idesc, (c.pos > 0 || kk > 0) ? 1u : 0u);
@@ -416,26 +637,47 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   } else if (warp < 6) {
     // ----------------------------------------- activation producers --
     // Lane l covers the 16-byte chunk l % 8 of B-tile rows l / 8 + 4 i.
-    constexpr int NPW = Cfg::kProducerWarps;  // this warp takes j = w4, w4 + NPW, ...
+    const int NPW = p.npw;                    // this warp takes j = w4, w4 + NPW, ...
     const int w4 = warp - 2;
     const int chunk = lane & 7;         // 16-byte chunk of the 128-wide K block
     const int row0 = lane >> 3;         // 0..3
+    // resident: the first ring's tiles were built in the prologue
+    const int j_first = w4 + (resident ? S : 0);
     TileCursor c;
-    c.init(u0, p.KB);
-    for (int k = 0; k < w4; ++k) c.next(p.KB, kpb, S);
-    for (int j = w4; w4 < NPW && j < J && ok; j += NPW) {
-      if (j > w4) {
+    c.init(nb0, kb0);
+    for (int k = 0; k < j_first; ++k) c.next(p.KB, kpb, S);
+    for (int j = j_first; w4 < NPW && j < J && ok; j += NPW) {
+      if (j > j_first) {
         for (int k = 0; k < NPW; ++k) c.next(p.KB, kpb, S);
       }
       const int s = c.s;
+      const int pos = c.pos;
+      uint8_t* btile = b_tiles + s * Cfg::kBTileBytes;
+      if (resident) {
+        // copy the prebuilt bytes once the MMA has released the stage
+        if (j >= S) ok = mbar_wait(&empty[s], c.ph ^ 1u, kSiteTmA);
+        if (!ok) break;
+        const int r = res_full ? c.kb : j;
+        const uint8_t* xq = x_tiles + static_cast<int64_t>(r) * p.M * 128 + chunk * 16;
+#pragma unroll
+        for (int i = 0; i < MT / 4; ++i) {
+          const int br = row0 + 4 * i;
+          const int m = br - pos * p.sw;
+          const bool live = m >= 0 && m < p.sw && m < p.M;
+          const uint4 packed = live ? *reinterpret_cast<const uint4*>(xq + m * 128) : make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(btile + br * 128 + ((chunk ^ (br & 7)) << 4)) = packed;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+        continue;
+      }
       ok = mbar_wait(&xfull[s], c.ph, kSiteTmA);
       if (!ok) break;
       const int nb = c.nb;
       const int kb = c.kb;
-      const int pos = c.pos;
-      uint8_t* stage = smem + s * Cfg::kStageBytes;
-      uint8_t* btile = stage + kTmATileBytes;
-      const __nv_bfloat16* xt = reinterpret_cast<const __nv_bfloat16*>(btile + Cfg::kBTileBytes);
+      const __nv_bfloat16* xt =
+          reinterpret_cast<const __nv_bfloat16*>(x_tiles + s * static_cast<uint32_t>(Cfg::kXTileBytes));
       float* sxs = sx_ring + (j & (kTmSxRing - 1)) * MT;
 #pragma unroll
       for (int i = 0; i < MT / 4; ++i) {
@@ -446,45 +688,22 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         if (__any_sync(0xffffffffu, live)) {   // rows of a lane octet are all live or all not
           float v[16];
           if (live) {
-            const __nv_bfloat16* xr = xt + m * 128 + chunk * 16;
+            const uint4* xp = reinterpret_cast<const uint4*>(xt + m * 128 + chunk * 16);
+            const uint4 xa = xp[0], xb = xp[1];
+            uint4 ua = xa, ub = xb;
             if constexpr (kSwiglu) {
-              const uint4* gp = reinterpret_cast<const uint4*>(xr);
-              const uint4* up = reinterpret_cast<const uint4*>(xr + p.x_tile_bytes / 2);
-              const uint4 g_a = gp[0], g_b = gp[1], u_a = up[0], u_b = up[1];
-              const uint32_t gw[8] = {g_a.x, g_a.y, g_a.z, g_a.w, g_b.x, g_b.y, g_b.z, g_b.w};
-              const uint32_t uw[8] = {u_a.x, u_a.y, u_a.z, u_a.w, u_b.x, u_b.y, u_b.z, u_b.w};
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                v[2 * e] = silu_mul(bf16_lo(gw[e]), bf16_lo(uw[e]));
-                v[2 * e + 1] = silu_mul(bf16_hi(gw[e]), bf16_hi(uw[e]));
-              }
-            } else {
-              const uint4* xp = reinterpret_cast<const uint4*>(xr);
-              const uint4 a = xp[0], b = xp[1];
-              const uint32_t xw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                v[2 * e] = bf16_lo(xw[e]);
-                v[2 * e + 1] = bf16_hi(xw[e]);
-              }
+              const uint4* up = reinterpret_cast<const uint4*>(xt + p.x_tile_bytes / 2 + m * 128 + chunk * 16);
+              ua = up[0];
+              ub = up[1];
             }
+            act16<kSwiglu>(v, xa, xb, ua, ub);
           } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] = 0.0f;
           }
-          float amax = 0.0f;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
-          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-          amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+          float sx;
+          packed = quant16_octet(v, live, sx);
           if (live) {
-            const float sx = group_scale(amax);
-            const float sinv = __frcp_rn(sx);
-            packed.x = quant_pair(v[0], v[1], sinv) | (static_cast<uint32_t>(quant_pair(v[2], v[3], sinv)) << 16);
-            packed.y = quant_pair(v[4], v[5], sinv) | (static_cast<uint32_t>(quant_pair(v[6], v[7], sinv)) << 16);
-            packed.z = quant_pair(v[8], v[9], sinv) | (static_cast<uint32_t>(quant_pair(v[10], v[11], sinv)) << 16);
-            packed.w = quant_pair(v[12], v[13], sinv) | (static_cast<uint32_t>(quant_pair(v[14], v[15], sinv)) << 16);
             if (chunk == 0) sxs[m] = sx;
             if (nb == 0) {
               if (p.xq_out)
@@ -514,7 +733,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     int seg_j0 = 0, seg_kb0 = 0;
     AccCursor accc;
     TileCursor cur;
-    cur.init(u0, p.KB);
+    cur.init(nb0, kb0);
     for (int j = 0; j < J; ++j, cur.next(p.KB, kpb, S)) {
       const int nb = cur.nb;
       const int kb = cur.kb;
@@ -529,18 +748,61 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const bool group_end = (pos == kpb - 1) || (kb == p.KB - 1) || (j == J - 1);
       if (!group_end) continue;
       const int a = accc.a;
+      const int jq0 = j - pos;                 // first K block of the group
+      const int rq0 = res_full ? kb - pos : jq0;   // its resident slot
+      // Column c of the group holds token m = c % sw of K block q = c / sw;
+      // its scale is sx[m, q] * ws[q].  All loads are in bounds (unused
+      // columns read entry 0) so they issue back to back; resident scales of
+      // the first kPre columns are loaded before the accumulator is ready.
+      auto col_scale = [&](int c, bool& use) {
+        const int q = c >> p.lg_sw;
+        const int m = c & (p.sw - 1);
+        use = q <= pos && m < p.M;
+        const int qc = use ? q : 0;
+        const int mc = use ? m : 0;
+        const int si = resident ? (rq0 + qc) * p.M + mc : ((jq0 + qc) & (kTmSxRing - 1)) * MT + mc;
+        return sx_ring[si] * ws_cache[jq0 + qc];
+      };
+      constexpr bool kPre = MT == 16;         // the 16-token tile: all scales in registers up front
+      float scl[16];
+      uint32_t pre_mask = 0;                   // bit c: column c holds a live (token, K block)
+      auto load_scales = [&]() {
+        if constexpr (kPre) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            bool u;
+            scl[c] = col_scale(c, u);
+            pre_mask |= u ? (1u << c) : 0u;
+          }
+        }
+      };
+      if (resident) load_scales();
       if (ok) ok = mbar_wait(&acc_full[a], accc.round, kSiteTmAcc);
-      if (lane == 0) {
+      if (!resident && lane == 0) {
         for (int q = 0; q <= pos && ok; ++q) ok = tag_wait(sx_tag + ((j - pos + q) & (kTmSxRing - 1)),
                                                          static_cast<uint32_t>(j - pos + q + 1));
         __threadfence_block();
       }
-      ok = __shfl_sync(0xffffffffu, ok, 0) != 0;
+      ok = __all_sync(0xffffffffu, ok) != 0;   // tcgen05.ld below is warp-collective
+      if (!resident) load_scales();
       tc_fence_after();
-      const int jq0 = j - pos;                 // first K block of the group
 #pragma unroll
       for (int c16 = 0; c16 < MT / 16; ++c16) {
         float v[16];
+        float sc[16];
+        uint32_t m16 = 0;
+        if constexpr (kPre) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sc[i] = scl[i];
+          m16 = pre_mask;
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            bool u;
+            sc[i] = col_scale(16 * c16 + i, u);
+            m16 |= u ? (1u << i) : 0u;
+          }
+        }
         if (ok) {
           tmem_ld16(tmem_base + t_lane + static_cast<uint32_t>(a * MT + 16 * c16), v);
         } else {
@@ -548,16 +810,8 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           for (int i = 0; i < 16; ++i) v[i] = 0.0f;
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c = 16 * c16 + i;
-          const int q = c >> p.lg_sw;
-          const int m = c & (p.sw - 1);
-          if (q <= pos && m < p.M) {
-            const float sxv = sx_ring[((jq0 + q) & (kTmSxRing - 1)) * MT + m];
-            const float wsv = ws_cache[jq0 + q];
-            acc[c] = fmaf(v[i], sxv * wsv, acc[c]);
-          }
-        }
+        for (int i = 0; i < 16; ++i)
+          if ((m16 >> i) & 1u) acc[16 * c16 + i] = fmaf(v[i], sc[i], acc[16 * c16 + i]);
       }
       tc_fence_before();
       __syncwarp();
@@ -577,6 +831,14 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
           for (int m = 0; m < MT; ++m)
             if (m < p.M) p.out[static_cast<int64_t>(m) * p.ldo + n] = __float2bfloat16_rn(acc[m]);
+        } else if (p.csize > 1) {
+          // cluster split-K: the partial sums stay in this CTA's shared memory
+          // (the A tiles are free: every MMA has completed) and are reduced
+          // across the cluster at the end of the kernel
+          float* part = reinterpret_cast<float*>(a_tiles);
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            if (m < p.M) part[m * 128 + row] = acc[m];
         } else {
           // partial row block: publish, count, and let the last CTA reduce
           const int slot = (seg_j0 == 0) ? 0 : 1;
@@ -621,6 +883,28 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   }
 
+  if (p.csize > 1) {
+    // Cluster split-K reduction.  The CTAs of a cluster are the csize K parts
+    // of one row block; after the barrier, epilogue thread t of cluster rank r
+    // reduces elements e = r*128 + t (+ 128*csize ...) of the [M][128] partial
+    // sums, reading every rank's value over distributed shared memory and
+    // adding them in rank order (the result does not depend on timing).
+    cluster_sync_all();
+    if (warp >= 6) {
+      const int rank = static_cast<int>(cluster_rank());
+      const int nbc = static_cast<int>(u0 / p.KB);
+      const float* part = reinterpret_cast<const float*>(a_tiles);
+      for (int e = rank * 128 + (tid - 192); e < p.M * 128; e += 128 * p.csize) {
+        float sum = 0.0f;
+#pragma unroll
+        for (int q = 0; q < kTmMaxCluster; ++q)
+          if (q < p.csize) sum += ld_dsmem(dsmem_addr(part + e, q));
+        p.out[static_cast<int64_t>(e >> 7) * p.ldo + nbc * 128 + (e & 127)] = __float2bfloat16_rn(sum);
+      }
+    }
+    cluster_sync_all();   // this CTA's shared memory stays until the cluster has read it
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -638,18 +922,17 @@ inline int tm_slots(int sm_count, int MT) { return sm_count * (MT == 16 ? tm_cta
 
 // Grid size.  Preferred: an aligned split -- every CTA takes one row block's
 // K range cut in S equal parts (S a power of two dividing K/128), so the
-// split-K hand-off involves only the S CTAs of a row block and S = 1 needs
-// none -- with NB * S the largest such count <= 1.3 x SMs (measured on B200:
-// about one CTA per SM with long K runs beats two with short runs plus
-// hand-offs).  Otherwise stream-K over all resident slots.
+// split-K hand-off involves only the S CTAs of a row block (a cluster when
+// S <= 8) and S = 1 needs none -- with NB * S the largest such count that
+// fits the resident CTA slots (measured on B200: with the cluster hand-off,
+// two CTAs per SM with short K runs beat one with long runs).  Otherwise
+// stream-K over all resident slots.
 inline int tm_grid(int64_t U, int sm_count, int MT, int NB = 0, int KB = 0) {
   const int64_t slots = tm_slots(sm_count, MT);
   if (NB > 0 && KB > 0) {
-    const int64_t cap = (static_cast<int64_t>(sm_count) * 13) / 10;
     int64_t best = 0;
     for (int S = 1; S <= KB; S *= 2)
-      if (KB % S == 0 && static_cast<int64_t>(NB) * S <= cap && static_cast<int64_t>(NB) * S <= slots)
-        best = static_cast<int64_t>(NB) * S;
+      if (KB % S == 0 && static_cast<int64_t>(NB) * S <= slots) best = static_cast<int64_t>(NB) * S;
     if (best >= sm_count / 2) return static_cast<int>(best);
   }
   return static_cast<int>(U < slots ? U : slots);
@@ -710,27 +993,87 @@ inline bool make_act_tmap(CUtensorMap* map, const void* x, int rows, int64_t col
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MT, bool S>
-int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int grid, int max_smem,
-                   cudaStream_t stream) {
-  using Cfg = TmCfg<MT, S>;
-  if (Cfg::kSmemBytes > static_cast<size_t>(max_smem)) return 8;  // FP8GQ_ERR_UNSUPPORTED
-  auto fn = gemm_tm_kernel<MT, S>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(Cfg::kSmemBytes)) != cudaSuccess)
+// Shared-memory plan of one pass: ring depth, activation mode and layout.
+struct TmPlan {
+  int stages, npw, resident;
+  uint32_t b_off, x_off, bar_off;
+  size_t smem;
+};
+
+// A grid of at most one CTA per SM (or a token tile that always runs one) gets
+// the SM's whole shared memory; otherwise the 16-token tile gets half.  The
+// resident activation mode -- M x (the CTA's K blocks) quantised bytes, their
+// scales in the sx ring -- is used when it still leaves at least 4 stages.
+template <int MT, bool SW>
+inline bool tm_plan(TmPlan* pl, int M, int64_t U, int64_t KB, int grid, int sm_count, int max_smem,
+                    int resident_mode) {
+  using Cfg = TmCfg<MT, SW>;
+  const bool one_per_sm = tm_ctas_per_sm<MT>() == 1 || grid <= sm_count;
+  int64_t budget = one_per_sm ? max_smem
+                              : static_cast<int64_t>(kTmSmemBudgetSm / tm_ctas_per_sm<MT>() - kTmSmemReservedPerCta);
+  if (budget > max_smem) budget = max_smem;
+  const int64_t avail = budget - static_cast<int64_t>(Cfg::kTailBytes + Cfg::kAlignSlack);
+  if (avail <= 0) return false;
+  const int64_t jmax = (U + grid - 1) / grid;
+  const int64_t nkb = jmax < KB ? jmax : KB;
+  int S = 0;
+  bool res = false;
+  int64_t xbytes = 0;
+  if (resident_mode != 0 && nkb * M <= static_cast<int64_t>(kTmSxRing) * MT) {
+    const int64_t rbytes = (nkb * M * 128 + 1023) / 1024 * 1024;
+    const int sr = tm_pick_stages((avail - rbytes) / (kTmATileBytes + Cfg::kBTileBytes));
+    if (sr >= 4) {
+      S = sr;
+      res = true;
+      xbytes = rbytes;
+    }
+  }
+  if (!res) {
+    S = tm_pick_stages(avail / (kTmATileBytes + Cfg::kBTileBytes + Cfg::kXTileBytes));
+    xbytes = static_cast<int64_t>(S) * Cfg::kXTileBytes;
+  }
+  if (S < 2) return false;
+  pl->stages = S;
+  pl->npw = tm_producer_warps(S);
+  pl->resident = res ? 1 : 0;
+  pl->b_off = static_cast<uint32_t>(S * kTmATileBytes);
+  pl->x_off = pl->b_off + static_cast<uint32_t>(S * Cfg::kBTileBytes);
+  pl->bar_off = pl->x_off + static_cast<uint32_t>(xbytes);
+  pl->smem = pl->bar_off + Cfg::kTailBytes + Cfg::kAlignSlack;
+  return pl->smem <= static_cast<size_t>(max_smem);
+}
+
+template <int MT, bool SW>
+int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int grid, int sm_count,
+                   int max_smem, cudaStream_t stream, int resident_mode, int csize) {
+  TmPlan pl;
+  if (!tm_plan<MT, SW>(&pl, p.M, p.U, p.KB, grid, sm_count, max_smem, resident_mode))
+    return 8;  // FP8GQ_ERR_UNSUPPORTED
+  auto fn = gemm_tm_kernel<MT, SW>;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess)
     return 7;  // FP8GQ_ERR_LAUNCH
-  p.stages = Cfg::kStages;
-  if (launch_with_pdl(fn, dim3(grid), dim3(kTmThreads), Cfg::kSmemBytes, stream, tw, tx, p) != cudaSuccess)
+  p.stages = pl.stages;
+  p.npw = pl.npw;
+  p.resident = pl.resident;
+  p.b_off = pl.b_off;
+  p.x_off = pl.x_off;
+  p.bar_off = pl.bar_off;
+  p.csize = csize;
+  if (launch_with_pdl_cluster(fn, dim3(grid), dim3(kTmThreads), pl.smem, stream, csize, tw, tx, p) != cudaSuccess)
     return 7;
   return cudaGetLastError() == cudaSuccess ? 0 : 7;
 }
 
 // Runs ceil(M / MT) passes of at most MT tokens; every pass reuses the
-// workspace (its counters are zero again when a pass ends).
+// workspace (its counters are zero again when a pass ends).  resident_mode 0
+// forces the streaming activation path (the resident one is used wherever it
+// fits otherwise); cluster_mode 0 forces the split-K hand-off through the
+// workspace (clusters are used for aligned splits of 2 to 8 CTAs otherwise).
 inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
                      int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
                      float* sx_out, void* workspace, size_t workspace_bytes, int sm_count, int max_smem,
-                     cudaStream_t stream, int early_weights = 0, int grid_override = 0) {
+                     cudaStream_t stream, int early_weights = 0, int grid_override = 0,
+                     int resident_mode = 1, int cluster_mode = 1) {
   const int MT = tm_token_tile(M);
   if (N / kGroup > kTmMaxRowBlocks) return 8;  // FP8GQ_ERR_UNSUPPORTED
   const size_t need = tm_workspace_bytes_for(M, N, K, sm_count);
@@ -752,6 +1095,11 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
                                       : tm_grid(p.U, sm_count, MT, N / kGroup, p.KB);
   if (grid > tm_slots(sm_count, MT)) return 8;  // partial-sum slots exist for at most this many CTAs
   if ((p.U + grid - 1) / grid + 1 > kTmWsCache) return 8;  // FP8GQ_ERR_UNSUPPORTED: tiles per CTA
+  // aligned split: every CTA takes 1/split of one row block's K range
+  const int NB = N / kGroup;
+  const int split = (grid % NB == 0) ? grid / NB : 0;
+  const bool aligned = split > 0 && p.KB % split == 0;
+  const int csize = (cluster_mode != 0 && aligned && split >= 2 && split <= kTmMaxCluster) ? split : 1;
   const int64_t xcols = swiglu ? 2 * static_cast<int64_t>(K) : K;
   for (int m0 = 0; m0 < M; m0 += MT) {
     const __nv_bfloat16* xp = static_cast<const __nv_bfloat16*>(x) + static_cast<int64_t>(m0) * ldx;
@@ -769,6 +1117,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     p.kpb = MT / sw;
     p.nacc = p.kpb >= 8 ? 2 : kTmMaxAcc;
     p.x_tile_bytes = static_cast<uint32_t>(p.M) * 256u;
+    p.x = xp;
+    p.ldx = ldx;
     p.early_weights = early_weights;
     p.xq_out = xq_out ? xq_out + static_cast<int64_t>(m0) * K : nullptr;
     p.sx_out = sx_out ? sx_out + static_cast<int64_t>(m0) * (K / kGroup) : nullptr;
@@ -776,14 +1126,14 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     if (!make_act_tmap(&tmap_x, xp, p.M, xcols, ldx)) return 7;
     int st;
     if (MT == 16)
-      st = swiglu ? launch_tm_pass<16, true>(tmap_w, tmap_x, p, grid, max_smem, stream)
-                  : launch_tm_pass<16, false>(tmap_w, tmap_x, p, grid, max_smem, stream);
+      st = swiglu ? launch_tm_pass<16, true>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize)
+                  : launch_tm_pass<16, false>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize);
     else if (MT == 32)
-      st = swiglu ? launch_tm_pass<32, true>(tmap_w, tmap_x, p, grid, max_smem, stream)
-                  : launch_tm_pass<32, false>(tmap_w, tmap_x, p, grid, max_smem, stream);
+      st = swiglu ? launch_tm_pass<32, true>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize)
+                  : launch_tm_pass<32, false>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize);
     else
-      st = swiglu ? launch_tm_pass<64, true>(tmap_w, tmap_x, p, grid, max_smem, stream)
-                  : launch_tm_pass<64, false>(tmap_w, tmap_x, p, grid, max_smem, stream);
+      st = swiglu ? launch_tm_pass<64, true>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize)
+                  : launch_tm_pass<64, false>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize);
     if (st) return st;
   }
   return 0;

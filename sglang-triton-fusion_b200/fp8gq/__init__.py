@@ -9,9 +9,11 @@ Entry points:
   patch_fp8_fused_tail             the sglang linear wrappers and install()
 The C ABI is include/fp8gq.h (libfp8gq.so next to this file).
 """
-from ._lib import Fp8gqError, device_error, load, set_static_weights  # noqa: F401
+from ._lib import (TM_STREAM_ACTIVATIONS, TM_WORKSPACE_SPLITK, Fp8gqError, device_error, load,  # noqa: F401
+                   set_static_weights, set_tm_options)
 from .ops import (GROUP, TM, ShapeError, fused_gemv_quant, fused_swiglu_q_gemm,  # noqa: F401
                   group_quant, swiglu_group_quant, workspace)
 
 __all__ = ["Fp8gqError", "ShapeError", "GROUP", "TM", "fused_gemv_quant", "fused_swiglu_q_gemm",
-           "group_quant", "swiglu_group_quant", "workspace", "load", "device_error", "set_static_weights"]
+           "group_quant", "swiglu_group_quant", "workspace", "load", "device_error", "set_static_weights",
+           "set_tm_options", "TM_STREAM_ACTIVATIONS", "TM_WORKSPACE_SPLITK"]

@@ -44,6 +44,7 @@ SIGNATURES = {
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
     "fp8gq_set_static_weights": (_I, [_I]),
+    "fp8gq_set_tm_options": (_I, [_I]),
     "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),
 }
 
@@ -101,6 +102,20 @@ def set_static_weights(enable: bool) -> bool:
     earlier on the calling stream (see fp8gq_set_static_weights in
     include/fp8gq.h).  Returns the previous setting."""
     return bool(load().fp8gq_set_static_weights(1 if enable else 0))
+
+
+TM_STREAM_ACTIVATIONS = 1   # FP8GQ_TM_STREAM_ACTIVATIONS
+TM_WORKSPACE_SPLITK = 2     # FP8GQ_TM_WORKSPACE_SPLITK
+
+
+def set_tm_options(flags: int) -> int:
+    """Tile-kernel strategy switches, a mask of TM_STREAM_ACTIVATIONS and
+    TM_WORKSPACE_SPLITK (0 = pick each strategy where it fits; see
+    fp8gq_set_tm_options in include/fp8gq.h).  Returns the previous mask."""
+    prev = load().fp8gq_set_tm_options(int(flags))
+    if prev < 0:
+        raise ValueError(f"unknown tile-kernel option bits in {flags!r}")
+    return prev
 
 
 def device_error(clear: bool = False) -> int:

@@ -125,7 +125,7 @@ def test_row_kernel_qwen3_8b(fp8gq, cuda_device, name):
     K, N = QWEN3_8B[name]
     x = gpu_activation(1, K, 1, cuda_device)
     wq, ws = gpu_weight(N, K, 2, cuda_device)
-    out, xq, sx = fp8gq.fused_gemv_quant(x, wq, ws, return_quant=True)
+    out, xq, sx = fp8gq.fused_gemv_quant(x, wq, ws, return_quant=True, kernel="row")
     _, exact, rq, rs = oracle_of(x, wq, ws)
     assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
     assert_close(to_f32(out), exact, 2.0)
@@ -210,6 +210,53 @@ def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
     assert_close(to_f32(a), exact, 3.0)
 
 
+@pytest.mark.parametrize("M, K, N, swiglu", [
+    (1, 4096, 24576, False),    # one CTA per row block, whole K range resident (slot = K block)
+    (1, 4096, 4096, False),     # K range split 8 ways: a cluster of 8 CTAs per row block (slot = tile)
+    (2, 4096, 6144, False),     # a cluster of 4
+    (3, 2560, 4096, False),
+    (4, 4096, 1280, False),     # split 16 ways: beyond a cluster, the hand-off goes through the workspace
+    (2, 10368, 896, False),     # stream-K: CTA ranges cross row blocks, K blocks wrap
+    (16, 1024, 1280, False),    # 16 tokens x 8 K blocks: a large resident footprint
+    (16, 4096, 6144, False),    # too large to be resident next to a 2-CTA-per-SM ring
+    (40, 2048, 2560, False),    # 64-token tile
+    (1, 12288, 4096, True),
+    (2, 12288, 4096, True),
+    (3, 2560, 2560, True),
+])
+def test_tile_kernel_strategies_agree(fp8gq, cuda_device, M, K, N, swiglu):
+    """The activation feed (resident / streaming) and the split-K reduction
+    (cluster / workspace) change where data waits, not what is
+    computed: the same MMAs on the same bytes, partial sums added in the same
+    order.  All combinations agree bit for bit, with each other and (quant
+    outputs) with the oracle."""
+    xb = gpu_activation(M, (2 * K if swiglu else K) + 64, 130 + M, cuda_device, std=1.5 if swiglu else 1.0,
+                        outliers=not swiglu)
+    x = xb[:, :2 * K] if swiglu else xb[:, :K]               # a row stride longer than the row
+    wq, ws = gpu_weight(N, K, 131, cuda_device)
+    run = fp8gq.fused_swiglu_q_gemm if swiglu else (lambda *a, **k: fp8gq.fused_gemv_quant(*a, kernel="tm", **k))
+    res = {}
+    for flags in (0, fp8gq.TM_STREAM_ACTIVATIONS, fp8gq.TM_WORKSPACE_SPLITK,
+                  fp8gq.TM_STREAM_ACTIVATIONS | fp8gq.TM_WORKSPACE_SPLITK):
+        prev = fp8gq.set_tm_options(flags)
+        try:
+            res[flags] = [t.clone() for t in run(x, wq, ws, return_quant=True)]
+        finally:
+            fp8gq.set_tm_options(prev)
+    for flags in list(res)[1:]:
+        for a, b in zip(res[0], res[flags]):
+            assert torch.equal(a, b), flags
+    _, exact, rq, rs = oracle_of(x.contiguous(), wq, ws, swiglu=swiglu)
+    out, xq, sx = res[0]
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert_close(to_f32(out), exact, 3.0)
+
+
+def test_tile_options_reject_unknown_bits(fp8gq, cuda_device):
+    with pytest.raises(ValueError):
+        fp8gq.set_tm_options(4)
+
+
 def test_tile_kernel_workspace_shared_across_shapes(fp8gq, cuda_device):
     """Small-N and large-N calls alternate on one workspace: the split-K
     counters of one shape must not be overwritten by another's partial sums."""
@@ -235,7 +282,8 @@ def test_swiglu_down_proj(fp8gq, cuda_device, M):
     out, xq, sx = fp8gq.fused_swiglu_q_gemm(gu, wq, ws, return_quant=True)
     _, exact, rq, rs = oracle_of(gu, wq, ws, swiglu=True)
     assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
-    assert_close(to_f32(out), exact, 2.0 if M == 1 else 3.0)
+    # 12288 -> 4096 is routed to the tile kernel at every M (its tolerance)
+    assert_close(to_f32(out), exact, 3.0)
 
 
 # ------------------------------------------ launch ordering (PDL) --------
