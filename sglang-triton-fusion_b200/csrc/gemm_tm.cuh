@@ -501,54 +501,77 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const int oct = (warp - 2) * 4 + (lane >> 3);
       const int chunk = lane & 7;
       const int ngroups = p.M * nkb;
-      for (int g0 = 0; g0 < ngroups; g0 += 32) {
-        const int g = g0 + oct;
-        const bool live = g < ngroups;
-        const int m = live ? g / nkb : 0;
-        const int r = live ? g - m * nkb : 0;
-        int kb = res_full ? r : kb0 + r;
+      // group g of this pass: token m = g / nkb, slot r = g % nkb, K block kb
+      auto group_of = [&](int g, int& m, int& r, int& kb) {
+        m = g / nkb;
+        r = g - m * nkb;
+        kb = res_full ? r : kb0 + r;
         if (kb >= p.KB) kb -= p.KB;
-        float v[16];
-        if (live) {
-          // L2-coherent loads: the activation may come from the kernel before
-          // this one in the stream
-          const __nv_bfloat16* xr = p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 + chunk * 16;
-          const uint4 xa = __ldcg(reinterpret_cast<const uint4*>(xr));
-          const uint4 xb = __ldcg(reinterpret_cast<const uint4*>(xr) + 1);
-          uint4 ua = xa, ub = xb;
-          if constexpr (kSwiglu) {
-            ua = __ldcg(reinterpret_cast<const uint4*>(xr + p.K));
-            ub = __ldcg(reinterpret_cast<const uint4*>(xr + p.K) + 1);
-          }
-          act16<kSwiglu>(v, xa, xb, ua, ub);
-        } else {
+      };
+      // The loads of kPasses passes are issued before any of them is
+      // quantised (L2-coherent loads: the activation may come from the kernel
+      // before this one in the stream), so a pass costs one L2 round trip per
+      // kPasses passes rather than one each.
+      constexpr int kPasses = kSwiglu ? 2 : 4;
+      constexpr int kWords = kSwiglu ? 4 : 2;
+      for (int g0 = 0; g0 < ngroups; g0 += 32 * kPasses) {
+        uint4 wd[kPasses][kWords];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+        for (int i = 0; i < kPasses; ++i) {
+          const int g = g0 + 32 * i + oct;
+          if (g < ngroups) {
+            int m, r, kb;
+            group_of(g, m, r, kb);
+            const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 +
+                                                             chunk * 16);
+            wd[i][0] = __ldcg(xr);
+            wd[i][1] = __ldcg(xr + 1);
+            if constexpr (kSwiglu) {
+              const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(xr) + p.K);
+              wd[i][kWords - 2] = __ldcg(ur);
+              wd[i][kWords - 1] = __ldcg(ur + 1);
+            }
+          }
         }
-        float sx;
-        const uint4 packed = quant16_octet(v, live, sx);
-        if (live) {
-          *reinterpret_cast<uint4*>(x_tiles + (static_cast<int64_t>(r) * p.M + m) * 128 + chunk * 16) = packed;
-          if (chunk == 0) sx_ring[r * p.M + m] = sx;
-          // first-ring tiles j < nfirst that use slot r: j = r (slot = tile),
-          // or j = r - kb0 mod KB and every KB after it (slot = K block)
-          int jj = r;
-          int step = nfirst;
-          if (res_full) {
-            jj = r - kb0;
-            if (jj < 0) jj += p.KB;
-            step = p.KB;
+#pragma unroll
+        for (int i = 0; i < kPasses; ++i) {
+          if (g0 + 32 * i >= ngroups) break;   // uniform across the warp
+          const int g = g0 + 32 * i + oct;
+          const bool live = g < ngroups;
+          int m = 0, r = 0, kb = 0;
+          if (live) group_of(g, m, r, kb);
+          float v[16];
+          if (live) {
+            act16<kSwiglu>(v, wd[i][0], wd[i][1], wd[i][kWords - 2], wd[i][kWords - 1]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = 0.0f;
           }
-          for (; jj < nfirst; jj += step) {
-            const int br = tile_pos(jj, kb0, p.KB, kpb) * p.sw + m;
-            *reinterpret_cast<uint4*>(b_tiles + jj * Cfg::kBTileBytes + br * 128 + ((chunk ^ (br & 7)) << 4)) =
-                packed;
-          }
-          if (kb >= u0 && kb < u1) {
-            // this CTA holds tile (row block 0, kb): it writes the optional outputs
-            if (p.xq_out)
-              *reinterpret_cast<uint4*>(p.xq_out + static_cast<int64_t>(m) * p.K + kb * 128 + chunk * 16) = packed;
-            if (p.sx_out && chunk == 0) p.sx_out[static_cast<int64_t>(m) * p.KB + kb] = sx;
+          float sx;
+          const uint4 packed = quant16_octet(v, live, sx);
+          if (live) {
+            *reinterpret_cast<uint4*>(x_tiles + (static_cast<int64_t>(r) * p.M + m) * 128 + chunk * 16) = packed;
+            if (chunk == 0) sx_ring[r * p.M + m] = sx;
+            // first-ring tiles j < nfirst that use slot r: j = r (slot = tile),
+            // or j = r - kb0 mod KB and every KB after it (slot = K block)
+            int jj = r;
+            int step = nfirst;
+            if (res_full) {
+              jj = r - kb0;
+              if (jj < 0) jj += p.KB;
+              step = p.KB;
+            }
+            for (; jj < nfirst; jj += step) {
+              const int br = tile_pos(jj, kb0, p.KB, kpb) * p.sw + m;
+              *reinterpret_cast<uint4*>(b_tiles + jj * Cfg::kBTileBytes + br * 128 + ((chunk ^ (br & 7)) << 4)) =
+                  packed;
+            }
+            if (kb >= u0 && kb < u1) {
+              // this CTA holds tile (row block 0, kb): it writes the optional outputs
+              if (p.xq_out)
+                *reinterpret_cast<uint4*>(p.xq_out + static_cast<int64_t>(m) * p.K + kb * 128 + chunk * 16) = packed;
+              if (p.sx_out && chunk == 0) p.sx_out[static_cast<int64_t>(m) * p.KB + kb] = sx;
+            }
           }
         }
       }
@@ -925,15 +948,19 @@ inline int tm_slots(int sm_count, int MT) { return sm_count * (MT == 16 ? tm_cta
 // split-K hand-off involves only the S CTAs of a row block (a cluster when
 // S <= 8) and S = 1 needs none -- with NB * S the largest such count that
 // fits the resident CTA slots (measured on B200: with the cluster hand-off,
-// two CTAs per SM with short K runs beat one with long runs).  Otherwise
-// stream-K over all resident slots.
+// two CTAs per SM with short K runs beat one with long runs), splits of at
+// most 8 preferred.  Otherwise stream-K over all resident slots.
 inline int tm_grid(int64_t U, int sm_count, int MT, int NB = 0, int KB = 0) {
   const int64_t slots = tm_slots(sm_count, MT);
   if (NB > 0 && KB > 0) {
-    int64_t best = 0;
-    for (int S = 1; S <= KB; S *= 2)
-      if (KB % S == 0 && static_cast<int64_t>(NB) * S <= slots) best = static_cast<int64_t>(NB) * S;
-    if (best >= sm_count / 2) return static_cast<int>(best);
+    // splits a cluster can reduce (S <= 8) first: the workspace hand-off of a
+    // wider split costs more than the extra CTAs gain
+    for (int max_split : {kTmMaxCluster, KB}) {
+      int64_t best = 0;
+      for (int S = 1; S <= KB && S <= max_split; S *= 2)
+        if (KB % S == 0 && static_cast<int64_t>(NB) * S <= slots) best = static_cast<int64_t>(NB) * S;
+      if (best >= sm_count / 2) return static_cast<int>(best);
+    }
   }
   return static_cast<int>(U < slots ? U : slots);
 }
