@@ -389,6 +389,18 @@ def run_ours(args):
                 tmb[f"{name}_M{M}"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
             del wl
         extra["tm_blocked_qwen3_4b"] = tmb
+        # stand-alone SwiGLU + quant writer on a prefill chunk (512 tokens x
+        # Qwen3-4B intermediate 9728), gate/up rotating through > L2
+        wr = []
+        for c in range(8):
+            gw = torch.randn(512, 2 * 9728, device=dev).bfloat16()
+            wr.append((gw[:, :9728], gw[:, 9728:]))
+        calls = [lambda p=p: fp8gq.fused_swiglu_quant(p[0], p[1]) for p in wr]
+        us = graph_us(calls)
+        b = 2 * 512 * 9728 * 2 + 512 * 9728 + 4 * 512 * 76
+        extra["swiglu_quant_writer_512x9728"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1),
+                                                 "bytes_per_call": b}
+        del wr
         torch.cuda.empty_cache()
 
     peak, peak_kind = measured_peak()

@@ -123,6 +123,25 @@ int fp8gq_group_quant(const void *x, int64_t ldx, int M, int K,
 int fp8gq_swiglu_group_quant(const void *gu, int64_t ldgu, int M, int I,
                              uint8_t *xq, float *sx, fp8gq_stream_t stream);
 
+/* Stand-alone SwiGLU writers for any M (the prefill side, M > 16), gate and up
+ * as separate bf16 [M, I] operands (row strides ldg, ldu elements, 16-byte
+ * aligned), I % 128 == 0:
+ *   y = g * sigmoid(g) * u in fp32 (sigmoid(g) = 1 / (1 + exp(-g)));
+ * fp8gq_swiglu stores bf16(y) (RNE) to out [M, I] (row stride ldo elements).
+ * Replaces fused_swiglu (kernels/fused_swiglu_fp8.py:19-27, :48-53). */
+int fp8gq_swiglu(const void *gate, int64_t ldg, const void *up, int64_t ldu, void *out, int64_t ldo,
+                 int M, int I, fp8gq_stream_t stream);
+
+/* fp8gq_swiglu_quant quantises y per row and 128-group with that module's own
+ * formula (not the GEMV prologue's):
+ *   scale = max(amax / 448, 1e-30),  q = e4m3_rne(clamp(y / scale, +-448))
+ * (IEEE divisions) into q uint8 [M, I] (row stride ldq bytes, 8-byte
+ * aligned) and scale fp32 [M, I/128] (contiguous).  Replaces
+ * fused_swiglu_quant / swiglu_quant_kernel (kernels/fused_swiglu_fp8.py:30-45,
+ * :56-63). */
+int fp8gq_swiglu_quant(const void *gate, int64_t ldg, const void *up, int64_t ldu, uint8_t *q, int64_t ldq,
+                       float *scale, int M, int I, fp8gq_stream_t stream);
+
 /* Declares (enable != 0) that weights and their block scales are never written
  * by work queued earlier on the stream of a call -- true in an inference server
  * whose weights are loaded once.  The kernels are launched with programmatic

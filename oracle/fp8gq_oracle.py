@@ -215,6 +215,37 @@ def swiglu_quant(gu: np.ndarray):
 
 
 # --------------------------------------------------------------------------
+# the stand-alone SwiGLU writers (kernels/fused_swiglu_fp8.py)
+# --------------------------------------------------------------------------
+
+WRITER_SCALE_FLOOR = np.float32(1e-30)
+
+
+def swiglu_writer(g: np.ndarray, u: np.ndarray) -> np.ndarray:
+    """fused_swiglu (kernels/fused_swiglu_fp8.py:19-27): y = g * sigmoid(g) * u
+    in fp32, stored as bf16 (RNE).  Returns the bf16 values as float32."""
+    return bf16_round(silu_mul(g, u))
+
+
+def swiglu_quant_writer(g: np.ndarray, u: np.ndarray):
+    """fused_swiglu_quant (kernels/fused_swiglu_fp8.py:30-45), a different
+    formula from the GEMV prologue's: per 128-group
+      scale = max(amax / 448, 1e-30)            (:41, IEEE division)
+      q     = e4m3_rne(clamp(y / scale, +-448)) (:42, IEEE division, no reciprocal)
+    g, u: float32 [M, I] (bf16 values), I % 128 == 0.
+    Returns (q uint8 [M, I], scale float32 [M, I/128], y float32 [M, I])."""
+    y = silu_mul(g, u)
+    M, I = y.shape
+    if I % GROUP:
+        raise ValueError("I must be a multiple of 128")
+    yg = y.reshape(M, I // GROUP, GROUP)
+    am = np.abs(yg).max(axis=-1).astype(np.float32)
+    scale = np.maximum((am / E4M3_MAX).astype(np.float32), WRITER_SCALE_FLOOR).astype(np.float32)
+    q = np.clip((yg / scale[..., None]).astype(np.float32), -E4M3_MAX, E4M3_MAX).astype(np.float32)
+    return e4m3_encode_rne(q).reshape(M, I), scale, y
+
+
+# --------------------------------------------------------------------------
 # block dequant and the contraction
 # --------------------------------------------------------------------------
 

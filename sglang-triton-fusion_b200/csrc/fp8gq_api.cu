@@ -11,6 +11,7 @@
 #include "gemm_tm.cuh"
 #include "gemv_row.cuh"
 #include "quant_only.cuh"
+#include "swiglu_writer.cuh"
 
 using namespace fp8gq;
 
@@ -168,6 +169,37 @@ int launch_quant(bool swiglu, const void* x, int64_t ldx, int M, int K, uint8_t*
   return launch_status();
 }
 
+int launch_swiglu_writer(bool quant, const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out,
+                         int64_t ldo, float* scale, int M, int I, cudaStream_t stream) {
+  DeviceInfo di;
+  int st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  const int64_t groups = static_cast<int64_t>(M) * (I / kGroup);
+  int64_t blocks = (groups + 15) / 16;
+  const int64_t cap = static_cast<int64_t>(di.sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  auto g = static_cast<const __nv_bfloat16*>(gate);
+  auto u = static_cast<const __nv_bfloat16*>(up);
+  cudaError_t e = quant ? launch_with_pdl(swiglu_writer_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256),
+                                          0, stream, g, ldg, u, ldu, out, ldo, scale, M, I)
+                        : launch_with_pdl(swiglu_writer_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256),
+                                          0, stream, g, ldg, u, ldu, out, ldo, scale, M, I);
+  if (e != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  return launch_status();
+}
+
+int check_swiglu_writer(const void* gate, int64_t ldg, const void* up, int64_t ldu, const void* out, int64_t ldo,
+                        int M, int I, int out_bytes) {
+  if (!gate || !up || !out) return FP8GQ_ERR_NULL_POINTER;
+  if (M < 1 || I <= 0 || I % kGroup) return FP8GQ_ERR_SHAPE;
+  if (ldg < I || ldu < I || ldo < I) return FP8GQ_ERR_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(gate) & 15u) || (reinterpret_cast<uintptr_t>(up) & 15u) || (ldg % 8) ||
+      (ldu % 8) || (reinterpret_cast<uintptr_t>(out) & (out_bytes == 2 ? 15u : 7u)) ||
+      ((ldo * out_bytes) % (out_bytes == 2 ? 16 : 8)))
+    return FP8GQ_ERR_ALIGNMENT;
+  return FP8GQ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -277,6 +309,23 @@ int fp8gq_swiglu_group_quant(const void* gu, int64_t ldgu, int M, int I, uint8_t
       (reinterpret_cast<uintptr_t>(sx) & 3u))
     return FP8GQ_ERR_ALIGNMENT;
   return launch_quant(true, gu, ldgu, M, I, xq, sx, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo, int M,
+                 int I, fp8gq_stream_t stream) {
+  const int st = check_swiglu_writer(gate, ldg, up, ldu, out, ldo, M, I, 2);
+  if (st != FP8GQ_OK) return st;
+  return launch_swiglu_writer(false, gate, ldg, up, ldu, out, ldo, nullptr, M, I,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_swiglu_quant(const void* gate, int64_t ldg, const void* up, int64_t ldu, uint8_t* q, int64_t ldq,
+                       float* scale, int M, int I, fp8gq_stream_t stream) {
+  int st = check_swiglu_writer(gate, ldg, up, ldu, q, ldq, M, I, 1);
+  if (st != FP8GQ_OK) return st;
+  if (!scale) return FP8GQ_ERR_NULL_POINTER;
+  if (reinterpret_cast<uintptr_t>(scale) & 3u) return FP8GQ_ERR_ALIGNMENT;
+  return launch_swiglu_writer(true, gate, ldg, up, ldu, q, ldq, scale, M, I, static_cast<cudaStream_t>(stream));
 }
 
 int fp8gq_set_static_weights(int enable) {

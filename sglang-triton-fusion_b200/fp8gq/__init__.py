@@ -6,14 +6,16 @@ Entry points:
   fused_gemv_quant(x, Wq, Ws)      M == 1 row kernel / M > 1 tcgen05 tile kernel
   fused_swiglu_q_gemm(gu, Wd, Ws)  SwiGLU + quant + down_proj GEMV
   group_quant(x), swiglu_group_quant(gu)   the activation quant alone
+  fused_swiglu(g, u), fused_swiglu_quant(g, u)   stand-alone SwiGLU writers (large M)
   patch_fp8_fused_tail             the sglang linear wrappers and install()
 The C ABI is include/fp8gq.h (libfp8gq.so next to this file).
 """
 from ._lib import (TM_STREAM_ACTIVATIONS, TM_WORKSPACE_SPLITK, Fp8gqError, device_error, load,  # noqa: F401
                    set_static_weights, set_tm_options)
-from .ops import (GROUP, TM, ShapeError, fused_gemv_quant, fused_swiglu_q_gemm,  # noqa: F401
-                  group_quant, swiglu_group_quant, workspace)
+from .ops import (GROUP, TM, ShapeError, fused_gemv_quant, fused_swiglu, fused_swiglu_q_gemm,  # noqa: F401
+                  fused_swiglu_quant, group_quant, swiglu_group_quant, workspace)
 
 __all__ = ["Fp8gqError", "ShapeError", "GROUP", "TM", "fused_gemv_quant", "fused_swiglu_q_gemm",
+           "fused_swiglu", "fused_swiglu_quant",
            "group_quant", "swiglu_group_quant", "workspace", "load", "device_error", "set_static_weights",
            "set_tm_options", "TM_STREAM_ACTIVATIONS", "TM_WORKSPACE_SPLITK"]

@@ -43,6 +43,8 @@ SIGNATURES = {
     "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "fp8gq_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _P]),
+    "fp8gq_swiglu_quant": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _P]),
     "fp8gq_set_static_weights": (_I, [_I]),
     "fp8gq_set_tm_options": (_I, [_I]),
     "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),

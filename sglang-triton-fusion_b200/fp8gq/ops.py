@@ -170,3 +170,41 @@ def swiglu_group_quant(gu: torch.Tensor):
     _lib.check(lib.fp8gq_swiglu_group_quant(_ptr(gu), gu.stride(0), M, I, _ptr(xq), _ptr(sx),
                                             _stream(gu.device)), "fp8gq_swiglu_group_quant")
     return xq, sx
+
+
+def _check_gate_up(gate: torch.Tensor, up: torch.Tensor):
+    _check_cuda(gate, up)
+    for t, n in ((gate, "gate"), (up, "up")):
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+            raise TypeError(f"{n} must be a 2-D bf16 tensor, contiguous along its last dimension")
+    if gate.shape != up.shape:
+        raise ShapeError(f"gate and up must have the same shape, got {tuple(gate.shape)} and {tuple(up.shape)}")
+    M, I = gate.shape
+    if I % GROUP:
+        raise ShapeError("the SwiGLU writers need I to be a multiple of 128")
+    return M, I
+
+
+def fused_swiglu(gate: torch.Tensor, up: torch.Tensor, *, out=None) -> torch.Tensor:
+    """gate, up: (M, I) bf16 -> bf16 silu(gate) * up, computed in fp32
+    (kernels/fused_swiglu_fp8.py:48-53)."""
+    M, I = _check_gate_up(gate, up)
+    if out is None:
+        out = torch.empty(M, I, dtype=torch.bfloat16, device=gate.device)
+    lib = _lib.load()
+    _lib.check(lib.fp8gq_swiglu(_ptr(gate), gate.stride(0), _ptr(up), up.stride(0), _ptr(out), out.stride(0),
+                                M, I, _stream(gate.device)), "fp8gq_swiglu")
+    return out
+
+
+def fused_swiglu_quant(gate: torch.Tensor, up: torch.Tensor):
+    """gate, up: (M, I) bf16 -> (q (M, I) float8_e4m3fn, scale (M, I/128) fp32)
+    with scale = max(amax / 448, 1e-30) and q = e4m3(clamp(y / scale))
+    (kernels/fused_swiglu_fp8.py:56-63)."""
+    M, I = _check_gate_up(gate, up)
+    q = torch.empty(M, I, dtype=torch.float8_e4m3fn, device=gate.device)
+    scale = torch.empty(M, I // GROUP, dtype=torch.float32, device=gate.device)
+    lib = _lib.load()
+    _lib.check(lib.fp8gq_swiglu_quant(_ptr(gate), gate.stride(0), _ptr(up), up.stride(0), _ptr(q), q.stride(0),
+                                      _ptr(scale), M, I, _stream(gate.device)), "fp8gq_swiglu_quant")
+    return q, scale

@@ -16,7 +16,8 @@ from tests._util import (assert_close, bf16_bits_tensor, bf16_tensor, f32_tensor
 
 pytestmark = pytest.mark.gpu
 
-GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith("writer_"))
+WRITER_GOLDEN = sorted((Path(__file__).parent / "golden").glob("writer_*.npz"))
 
 # Qwen3-8B decode linears (K, N) and Qwen3-4B tile shapes
 QWEN3_8B = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 24576), "down": (12288, 4096)}
@@ -284,6 +285,74 @@ def test_swiglu_down_proj(fp8gq, cuda_device, M):
     assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
     # 12288 -> 4096 is routed to the tile kernel at every M (its tolerance)
     assert_close(to_f32(out), exact, 3.0)
+
+
+# ---------------------------------------- stand-alone SwiGLU writers --
+
+@pytest.mark.parametrize("M, I", [(512, 9728), (16, 9728), (3, 256), (1, 12288)])
+def test_swiglu_writers_bit_exact(fp8gq, cuda_device, M, I):
+    g = gpu_activation(M, I, 200 + M, cuda_device, std=1.5, outliers=False)
+    u = gpu_activation(M, I, 300 + M, cuda_device, std=1.5, outliers=False)
+    q, scale = fp8gq.fused_swiglu_quant(g, u)
+    y = fp8gq.fused_swiglu(g, u)
+    rq, rs, _ = O.swiglu_quant_writer(to_f32(g), to_f32(u))
+    assert np.array_equal(to_u8(q), rq)
+    assert np.array_equal(to_f32(scale), rs)
+    assert np.array_equal(to_f32(y), O.swiglu_writer(to_f32(g), to_f32(u)))
+
+
+def test_swiglu_writers_on_gate_up_halves(fp8gq, cuda_device):
+    """gate and up as the two halves of one gate_up output (row stride 2I)."""
+    M, I = 40, 1024
+    gu = gpu_activation(M, 2 * I, 17, cuda_device, std=1.5, outliers=False)
+    g, u = gu[:, :I], gu[:, I:]
+    q, scale = fp8gq.fused_swiglu_quant(g, u)
+    rq, rs, _ = O.swiglu_quant_writer(to_f32(g), to_f32(u))
+    assert np.array_equal(to_u8(q), rq) and np.array_equal(to_f32(scale), rs)
+    out = torch.full((M, I + 64), 7.0, dtype=torch.bfloat16, device=cuda_device)
+    fp8gq.fused_swiglu(g, u, out=out[:, :I])
+    assert np.array_equal(to_f32(out[:, :I]), O.swiglu_writer(to_f32(g), to_f32(u)))
+    assert torch.all(out[:, I:] == 7.0)
+
+
+@pytest.mark.parametrize("path", WRITER_GOLDEN, ids=[p.stem for p in WRITER_GOLDEN])
+def test_swiglu_writer_golden_fixtures(fp8gq, cuda_device, path):
+    """The reference's own fused_swiglu / fused_swiglu_quant outputs."""
+    d = np.load(path)
+    g = bf16_bits_tensor(d["g_bf16"], cuda_device)
+    u = bf16_bits_tensor(d["u_bf16"], cuda_device)
+    q, scale = fp8gq.fused_swiglu_quant(g, u)
+    y = fp8gq.fused_swiglu(g, u)
+    assert np.array_equal(to_u8(q), d["q"])
+    assert np.array_equal(to_f32(y).view(np.uint32) >> 16, d["y_bf16"].astype(np.uint32))
+    assert np.allclose(to_f32(scale), d["scale"], rtol=2.0 ** -22, atol=0.0)
+
+
+def test_swiglu_writer_stress_battery(fp8gq, cuda_device):
+    """benchmarks/stress_tests.py:148-199 on the GPU writers."""
+    I = 9728
+    g = gpu_activation(8, I, 1, cuda_device, outliers=False)
+    u = gpu_activation(8, I, 2, cuda_device, outliers=False)
+    q1, s1 = fp8gq.fused_swiglu_quant(g, u)
+    q2, s2 = fp8gq.fused_swiglu_quant(g, u)
+    assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8)) and torch.equal(s1, s2)
+    z = torch.zeros(4, I, dtype=torch.bfloat16, device=cuda_device)
+    q, s = fp8gq.fused_swiglu_quant(z, z)
+    assert bool((q.view(torch.uint8) == 0).all()) and bool((s == 1e-30).all())
+    t = torch.full((2, I), 20.0, dtype=torch.bfloat16, device=cuda_device)
+    q, s = fp8gq.fused_swiglu_quant(t, t)
+    assert abs(q.float().abs().max().item() - 448.0) < 1e-2
+    n = torch.full((2, I), -50.0, dtype=torch.bfloat16, device=cuda_device)
+    out = fp8gq.fused_swiglu(n, u[:2])
+    ref = torch.nn.functional.silu(n.float()) * u[:2].float()
+    assert bool(torch.isfinite(out).all()) and torch.allclose(out.float(), ref, rtol=1e-2, atol=1e-2)
+    g10, u10 = g[:4] * 10, u[:4] * 10
+    q, s = fp8gq.fused_swiglu_quant(g10, u10)
+    y = torch.nn.functional.silu(g10.float()) * u10.float()
+    am = y.abs().view(4, -1, 128).amax(-1)
+    ns = (am / 448.0).clamp_min(1e-30)
+    nq = (y.view(4, -1, 128) / ns.unsqueeze(-1)).clamp(-448, 448).view(4, -1).to(torch.float8_e4m3fn)
+    assert (q.view(torch.uint8) == nq.view(torch.uint8)).float().mean().item() > 0.999
 
 
 # ------------------------------------------ launch ordering (PDL) --------

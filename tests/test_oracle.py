@@ -9,7 +9,8 @@ import torch
 
 from oracle import fp8gq_oracle as O
 
-GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith("writer_"))
+WRITER_GOLDEN = sorted((Path(__file__).parent / "golden").glob("writer_*.npz"))
 
 
 def test_golden_fixtures_present():
@@ -125,6 +126,59 @@ def test_determinism():
     a = O.group_quant(x)
     b = O.group_quant(x.copy())
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+
+
+# ------------------------------------------ stand-alone SwiGLU writers --
+
+def test_writer_fixtures_present():
+    assert {p.stem for p in WRITER_GOLDEN} == {"writer_grid", "writer_rand", "writer_extreme", "writer_zero",
+                                                "writer_sat"}
+
+
+@pytest.mark.parametrize("path", WRITER_GOLDEN, ids=[p.stem for p in WRITER_GOLDEN])
+def test_writer_oracle_matches_reference_kernels(path):
+    """kernels/fused_swiglu_fp8.py's fused_swiglu and fused_swiglu_quant (run in
+    Triton's CPU interpreter) against the oracle: every e4m3 code and every
+    bf16 output equal; scales equal, or within one fp32 ulp where the
+    reference's exp and the oracle's differ in the last bit (its own test
+    allows rtol 1e-5, kernels/fused_swiglu_fp8.py:99-100)."""
+    d = np.load(path)
+    g, u = O.bf16_from_bits(d["g_bf16"]), O.bf16_from_bits(d["u_bf16"])
+    q, scale, _ = O.swiglu_quant_writer(g, u)
+    assert np.array_equal(q, d["q"])
+    assert np.array_equal(O.bf16_bits(O.swiglu_writer(g, u)), d["y_bf16"])
+    assert np.allclose(scale, d["scale"], rtol=2.0 ** -22, atol=0.0)
+    if path.stem in ("writer_grid", "writer_zero", "writer_sat"):
+        assert np.array_equal(scale, d["scale"])      # exact inputs: exact scales
+
+
+def test_writer_known_answers():
+    """benchmarks/stress_tests.py:159-176: all-zero input gives q = 0 and the
+    1e-30 scale floor; gate = up = 20 reaches exactly |q| = 448."""
+    z = np.zeros((2, 256), np.float32)
+    q, s, _ = O.swiglu_quant_writer(z, z)
+    assert np.all(q == 0) and np.all(s == np.float32(1e-30))
+    t = np.full((2, 256), 20.0, np.float32)
+    q, s, _ = O.swiglu_quant_writer(t, t)
+    assert np.max(np.abs(O.E4M3_TABLE[q])) == 448.0
+
+
+def test_writer_formula_differs_from_gemv_prologue():
+    """The writer divides by the scale (kernels/fused_swiglu_fp8.py:42); the
+    GEMV prologue multiplies by its rounded reciprocal
+    (kernels/fused_gemv_quant.py:42) and floors amax at 1e-10 where the writer
+    floors the scale at 1e-30.  Both differences change codes, which is why
+    the two quantisers are kept apart."""
+    f = np.float32
+    y, sc = f(57.31668472290039), f(2.729365825653076)
+    div = f(y / sc)                          # 21.0 exactly: a tie, RNE -> 20
+    rcp = f(y * f(f(1.0) / sc))              # 21.000002 -> 22
+    assert div == f(21.0) and rcp > div
+    assert O.e4m3_encode_rne(np.array([div]))[0] != O.e4m3_encode_rne(np.array([rcp]))[0]
+    tiny = np.full((1, 128), 1e-12, np.float32)     # amax below the prologue's 1e-10 floor
+    qw, sw, _ = O.swiglu_quant_writer(np.full((1, 128), 30.0, np.float32), tiny)
+    qg, sg = O.group_quant(O.silu_mul(np.full((1, 128), 30.0, np.float32), tiny))
+    assert sw[0, 0] != sg[0, 0] and qw[0, 0] != qg[0, 0]
 
 
 def test_torch_reference_path_agrees_with_oracle():
