@@ -85,6 +85,9 @@ def parse():
     ap.add_argument("--static-weights", type=int, default=0,
                     help="1: declare the weights static (fp8gq.set_static_weights), letting each "
                          "kernel prefetch its first weight tiles before the previous one finishes")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: the kernels store their output slices into every rank's buffer over "
+                         "NVLink (p2p, default), or an NCCL all-gather follows every linear (nccl)")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
@@ -278,14 +281,28 @@ def run_ours(args):
         layers.append(lin)
     torch.cuda.synchronize()
 
+    pg = None
+    if world > 1 and args.gather == "p2p":
+        from fp8gq.dist import PeerGather
+        pg = PeerGather(out_all.view(-1))
+        # descriptors of every linear's output slice, built once (each call
+        # waits for the previous linear's slices, as a decoder's next linear
+        # would for its input)
+        descs = [[pg.descriptor(lin[i][6], rank * (lin[i][2] // world), True) for i in range(len(SHAPES))]
+                 for lin in layers]
+
     def step():
-        for lin in layers:
-            for name, K, N, wq, ws, x, out, shard in lin:
+        for li, lin in enumerate(layers):
+            for i, (name, K, N, wq, ws, x, out, shard) in enumerate(lin):
                 if world == 1:
                     fp8gq.fused_gemv_quant(x, wq, ws, out=out)
+                elif pg is not None:
+                    pg.linear(x, wq, ws, out, desc=descs[li][i])
                 else:
                     fp8gq.fused_gemv_quant(x, wq, ws, out=shard)
                     dist.all_gather_into_tensor(out.view(-1), shard.view(-1))
+        if pg is not None:
+            pg.wait(layers[-1][-1][6])      # the step ends when the last slices have landed
 
     for _ in range(max(args.warmup, 3)):
         step()
@@ -326,7 +343,7 @@ def run_ours(args):
         ms = float(t.item())
     clocks = sampler.summary()
     value = STEP_BYTES / (ms * 1e-3) / 1e9
-    launches = LAYERS * len(SHAPES) * args.steps
+    launches = (LAYERS * len(SHAPES) + (1 if pg is not None else 0)) * args.steps
 
     # ---- per-linear device time: graph of the 36 launches of one shape
     def graph_us(calls, reps=20):
@@ -389,6 +406,19 @@ def run_ours(args):
                 tmb[f"{name}_M{M}"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
             del wl
         extra["tm_blocked_qwen3_4b"] = tmb
+        # lm_head of Qwen3-8B (151936 x 4096, 622 MB of e4m3), two weight copies
+        lm = [make_weight_gpu(151936, 4096, seed=900 + c, dev=dev) for c in range(2)]
+        lmh = {}
+        for M in (1, 4):
+            xm = torch.randn(M, 4096, device=dev).bfloat16()
+            om = torch.empty(M, 151936, dtype=torch.bfloat16, device=dev)
+            calls = [lambda w=w: fp8gq.fused_gemv_quant(xm, w[0], w[1], out=om) for w in lm]
+            us = graph_us(calls, reps=20)
+            b = alg_bytes(M, 4096, 151936)
+            lmh[f"M{M}"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1), "bytes_per_call": b}
+        extra["lm_head_qwen3_8b"] = lmh
+        del lm
+        torch.cuda.empty_cache()
         # stand-alone SwiGLU + quant writer on a prefill chunk (512 tokens x
         # Qwen3-4B intermediate 9728), gate/up rotating through > L2
         wr = []
@@ -440,6 +470,8 @@ def run_ours(args):
     assert fp8gq.device_error() == 0, "a kernel recorded a wait timeout"
     del graph
     barrier()
+    if pg is not None:
+        pg.close()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -454,7 +486,9 @@ def run_ours(args):
                 "config": {"workload": WORKLOAD, "M": 1, "layers": LAYERS,
                            "bytes_per_step": STEP_BYTES,
                            "l2": "inputs larger than L2 (6.95 GB of weights per step, 126 MB L2)",
-                           "parallelism": f"N-sharded x{world} + NCCL all-gather per linear" if world > 1
+                           "parallelism": (f"N-sharded x{world}, output slices stored into every rank by the "
+                                           "kernels over NVLink" if pg is not None else
+                                           f"N-sharded x{world} + NCCL all-gather per linear") if world > 1
                            else "single GPU", "timing": "CUDA graph of one step, CUDA events",
                            "static_weights": bool(args.static_weights)},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},

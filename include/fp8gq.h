@@ -123,6 +123,56 @@ int fp8gq_group_quant(const void *x, int64_t ldx, int M, int K,
 int fp8gq_swiglu_group_quant(const void *gu, int64_t ldgu, int M, int I,
                              uint8_t *xq, float *sx, fp8gq_stream_t stream);
 
+/* N-sharded linears over several GPUs (one process per GPU): each rank runs
+ * the fused op on its rows [col0, col0 + N) of the weight, and the kernel
+ * writes that output slice into the same columns of every rank's full output
+ * buffer itself -- plain stores over NVLink through the peers' mapped
+ * pointers -- instead of a separate all-gather.  The last CTA then raises this
+ * rank's flag on every rank; a later call with wait_input != 0 (one whose
+ * activation is such a gathered output) waits, inside its kernel, until every
+ * rank's flag has caught up before it reads the activation.  The waits are
+ * bounded (FP8GQ_ERR_DEVICE_TIMEOUT through fp8gq_device_error).
+ *
+ * Every rank must issue the same sequence of gathered calls.  out[r] and
+ * flags[r] are rank r's buffers as mapped into this process (fp8gq_ipc_open;
+ * out[rank] and flags[rank] are this rank's own).  counter and seq are this
+ * rank's own, zero-filled once before the first call.  No counterpart in the
+ * reference (which is single-GPU); it replaces the NCCL all-gather after each
+ * linear of an N-sharded decoder. */
+#define FP8GQ_MAX_GATHER_RANKS 8
+typedef struct fp8gq_gather {
+    void *out[FP8GQ_MAX_GATHER_RANKS];       /* bf16 [M, ldo] full output of rank r */
+    uint32_t *flags[FP8GQ_MAX_GATHER_RANKS]; /* uint32 [world] flag array of rank r */
+    uint32_t *counter;                       /* this rank: one uint32, zero-filled */
+    uint32_t *seq;                           /* this rank: one uint32, zero-filled */
+    int64_t ldo;                             /* row stride of the full outputs, elements */
+    int col0;                                /* first column of this rank's slice */
+    int world;                               /* 2 .. FP8GQ_MAX_GATHER_RANKS */
+    int rank;
+    int wait_input;
+} fp8gq_gather;
+
+/* fp8gq_fused_gemv_quant with the output gathered as above (routing and
+ * workspace as fp8gq_fused_gemv_quant; N is this rank's slice width). */
+int fp8gq_fused_gemv_quant_gather(const void *x, int64_t ldx, const void *w, int64_t ldw,
+                                  const float *ws, int64_t ldws, int M, int N, int K,
+                                  const fp8gq_gather *gather, void *workspace, size_t workspace_bytes,
+                                  fp8gq_stream_t stream);
+
+/* Waits on `stream` (a one-thread kernel, bounded) until every rank's slice of
+ * this rank's last gathered output has arrived -- e.g. before the full output
+ * is read by something that is not a gathered call with wait_input set. */
+int fp8gq_gather_wait(const fp8gq_gather *gather, fp8gq_stream_t stream);
+
+/* Device-memory mapping between the processes of one node (CUDA IPC).
+ * fp8gq_ipc_get: a 64-byte handle of the allocation that holds `ptr`, and
+ * ptr's byte offset in it.  fp8gq_ipc_open: map a peer's handle (the current
+ * device gets peer access on first use) and return the mapped base and
+ * base + offset.  fp8gq_ipc_close: unmap a base returned by fp8gq_ipc_open. */
+int fp8gq_ipc_get(const void *ptr, void *handle64, uint64_t *offset);
+int fp8gq_ipc_open(const void *handle64, uint64_t offset, void **base, void **ptr);
+int fp8gq_ipc_close(void *base);
+
 /* Stand-alone SwiGLU writers for any M (the prefill side, M > 16), gate and up
  * as separate bf16 [M, I] operands (row strides ldg, ldu elements, 16-byte
  * aligned), I % 128 == 0:

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/fp8gq.h"
@@ -105,7 +106,8 @@ bool m1_uses_row(int N, int K) { return K <= kRowMaxK && static_cast<int64_t>(N)
 constexpr int kRowRingBytes = 96 * 1024;    // per CTA; two CTAs per SM
 
 int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const float* ws, int64_t ldws,
-               void* out, int N, int K, uint8_t* xq_out, float* sx_out, cudaStream_t stream) {
+               void* out, int N, int K, uint8_t* xq_out, float* sx_out, cudaStream_t stream,
+               const GatherParams* gather = nullptr) {
   DeviceInfo di;
   int dev = 0;
   int st = device_info(&di, &dev);
@@ -145,6 +147,7 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   p.stages = stages;
   p.xq_out = xq_out;
   p.sx_out = sx_out;
+  p.gather = gather ? *gather : GatherParams{};
   p.early_weights = g_static_weights.load(std::memory_order_relaxed);
   int grid = 2 * di.sm_count;
   if (grid > p.n_groups) grid = p.n_groups;
@@ -198,6 +201,53 @@ int check_swiglu_writer(const void* gate, int64_t ldg, const void* up, int64_t l
       ((ldo * out_bytes) % (out_bytes == 2 ? 16 : 8)))
     return FP8GQ_ERR_ALIGNMENT;
   return FP8GQ_OK;
+}
+
+// Waits (bounded) until every rank's slice of this rank's last gathered
+// output has arrived; one thread.
+__global__ void gather_wait_kernel(const GatherParams g) {
+  grid_dependency_wait();
+  if (threadIdx.x == 0) gather_wait_input(g);
+  grid_launch_dependents();
+}
+
+int to_gather_params(const fp8gq_gather* gather, GatherParams* g) {
+  if (!gather || !gather->counter || !gather->seq) return FP8GQ_ERR_NULL_POINTER;
+  if (gather->world < 2 || gather->world > FP8GQ_MAX_GATHER_RANKS || gather->rank < 0 ||
+      gather->rank >= gather->world || gather->col0 < 0 || gather->ldo < 1)
+    return FP8GQ_ERR_SHAPE;
+  *g = GatherParams{};
+  for (int r = 0; r < gather->world; ++r) {
+    if (!gather->out[r] || !gather->flags[r]) return FP8GQ_ERR_NULL_POINTER;
+    if ((reinterpret_cast<uintptr_t>(gather->out[r]) & 1u) || (reinterpret_cast<uintptr_t>(gather->flags[r]) & 3u))
+      return FP8GQ_ERR_ALIGNMENT;
+    g->out[r] = static_cast<__nv_bfloat16*>(gather->out[r]);
+    g->flags[r] = gather->flags[r];
+  }
+  g->counter = gather->counter;
+  g->seq = gather->seq;
+  g->ldo = gather->ldo;
+  g->col0 = gather->col0;
+  g->world = gather->world;
+  g->rank = gather->rank;
+  g->wait_input = gather->wait_input ? 1 : 0;
+  return FP8GQ_OK;
+}
+
+using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+// cuMemGetAddressRange, resolved through the runtime (no -lcuda at link time).
+AddressRangeFn address_range_fn() {
+  static std::once_flag once;
+  static AddressRangeFn fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(ptr);
+  });
+  return fn;
 }
 
 }  // namespace
@@ -309,6 +359,68 @@ int fp8gq_swiglu_group_quant(const void* gu, int64_t ldgu, int M, int I, uint8_t
       (reinterpret_cast<uintptr_t>(sx) & 3u))
     return FP8GQ_ERR_ALIGNMENT;
   return launch_quant(true, gu, ldgu, M, I, xq, sx, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_fused_gemv_quant_gather(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
+                                  int64_t ldws, int M, int N, int K, const fp8gq_gather* gather,
+                                  void* workspace, size_t workspace_bytes, fp8gq_stream_t stream) {
+  GatherParams g;
+  int st = to_gather_params(gather, &g);
+  if (st != FP8GQ_OK) return st;
+  if (gather->ldo < static_cast<int64_t>(gather->col0) + N) return FP8GQ_ERR_STRIDE;
+  // the rank's own output slice stands in for `out` in the shape checks
+  void* own = static_cast<__nv_bfloat16*>(gather->out[gather->rank]) + gather->col0;
+  st = check_common(x, w, ws, own, M, N, K, ldw, ldws, gather->ldo);
+  if (st != FP8GQ_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 1 && m1_uses_row(N, K)) return launch_row(false, x, w, ldw, ws, ldws, own, N, K, nullptr, nullptr, s, &g);
+  if (ldx < K || (ldx % 8) != 0) return ldx < K ? FP8GQ_ERR_STRIDE : FP8GQ_ERR_ALIGNMENT;
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  return launch_tm(false, x, ldx, w, ldw, ws, ldws, own, gather->ldo, M, N, K, nullptr, nullptr, workspace,
+                   workspace_bytes, di.sm_count, di.max_smem_optin, s, g_static_weights.load(std::memory_order_relaxed),
+                   0, tm_resident_mode(), tm_cluster_mode(), &g);
+}
+
+int fp8gq_gather_wait(const fp8gq_gather* gather, fp8gq_stream_t stream) {
+  GatherParams g;
+  int st = to_gather_params(gather, &g);
+  if (st != FP8GQ_OK) return st;
+  if (launch_with_pdl(gather_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), g) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  return launch_status();
+}
+
+int fp8gq_ipc_get(const void* ptr, void* handle64, uint64_t* offset) {
+  if (!ptr || !handle64 || !offset) return FP8GQ_ERR_NULL_POINTER;
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+  auto range = address_range_fn();
+  if (!range) return FP8GQ_ERR_DEVICE;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return FP8GQ_ERR_DEVICE;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return FP8GQ_ERR_DEVICE;
+  std::memcpy(handle64, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return FP8GQ_OK;
+}
+
+int fp8gq_ipc_open(const void* handle64, uint64_t offset, void** base, void** ptr) {
+  if (!handle64 || !base || !ptr) return FP8GQ_ERR_NULL_POINTER;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  void* b = nullptr;
+  if (cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return FP8GQ_ERR_DEVICE;
+  *base = b;
+  *ptr = static_cast<uint8_t*>(b) + offset;
+  return FP8GQ_OK;
+}
+
+int fp8gq_ipc_close(void* base) {
+  if (!base) return FP8GQ_ERR_NULL_POINTER;
+  return cudaIpcCloseMemHandle(base) == cudaSuccess ? FP8GQ_OK : FP8GQ_ERR_DEVICE;
 }
 
 int fp8gq_swiglu(const void* gate, int64_t ldg, const void* up, int64_t ldu, void* out, int64_t ldo, int M,

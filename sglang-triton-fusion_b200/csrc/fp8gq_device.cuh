@@ -30,6 +30,7 @@ enum ErrorSite : unsigned int {
   kSiteTmAcc = 5,
   kSiteTmTmem = 6,
   kSiteTmFixup = 7,      // tile kernel split-K partial-sum hand-off
+  kSiteGather = 8,       // waiting for the peers' output slices of a gathered linear
 };
 
 __device__ __forceinline__ void record_error(unsigned int site) {
@@ -213,6 +214,84 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   const float e = exp_cw(-g);
   const float s = __frcp_rn(__fadd_rn(1.0f, e));
   return __fmul_rn(__fmul_rn(g, s), u);
+}
+
+// ---------------------------------------------------------------------------
+// N-sharded output gather over peer memory (one process per GPU, NVLink)
+// ---------------------------------------------------------------------------
+constexpr int kMaxGatherRanks = 8;
+
+// A kernel with world > 0 writes its output slice (columns col0 .. col0 + N)
+// into the same columns of every rank's full output buffer -- plain stores
+// through the peers' mapped pointers -- and its last CTA then raises this
+// rank's flag on every rank to the rank's new sequence number.  A kernel with
+// wait_input set reads its activation only after every rank's flag has
+// reached this rank's sequence number, i.e. after every slice of the last
+// gathered output has landed here.  All ranks run the same sequence of
+// gathered kernels, so their sequence numbers advance together.
+struct GatherParams {
+  __nv_bfloat16* out[kMaxGatherRanks];   // rank r's full output [M, ldo], as mapped here
+  unsigned int* flags[kMaxGatherRanks];  // rank r's flags[world], as mapped here
+  unsigned int* counter;                 // this rank: CTAs of the running kernel that are done
+  unsigned int* seq;                     // this rank: sequence number of its last gathered kernel
+  int64_t ldo;
+  int col0;                              // first column of this rank's slice
+  int world;                             // 0: no gather (plain local output)
+  int rank;
+  int wait_input;
+};
+
+__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Output element (m, n) of this rank's slice, to every rank.
+__device__ __forceinline__ void gather_store(const GatherParams& g, int64_t m, int64_t n, __nv_bfloat16 v) {
+  const int64_t off = m * g.ldo + g.col0 + n;
+#pragma unroll 1
+  for (int r = 0; r < g.world; ++r) g.out[r][off] = v;
+}
+
+// One thread per CTA, after a barrier that follows every gather_store of the
+// CTA: count the CTA (acq_rel at GPU scope: the barrier puts the CTA's stores
+// before the release); the last one, having acquired every other CTA's count,
+// publishes the slice to every rank with a system-scope release, which by
+// cumulativity covers the stores of all CTAs.
+__device__ __forceinline__ void gather_cta_done(const GatherParams& g, unsigned int ncta) {
+  unsigned int old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(g.counter) : "memory");
+  if (old == ncta - 1u) {
+    *g.counter = 0u;                     // ready for the next gathered kernel on this stream
+    const unsigned int s = *g.seq + 1u;
+    *g.seq = s;
+#pragma unroll 1
+    for (int r = 0; r < g.world; ++r) st_release_sys_u32(g.flags[r] + g.rank, s);
+  }
+}
+
+// One thread, after grid_dependency_wait: wait (bounded) until every rank's
+// slice of this rank's last gathered output has arrived.  False (and the
+// error word set) on timeout.
+__device__ __forceinline__ bool gather_wait_input(const GatherParams& g) {
+  const unsigned int s = *reinterpret_cast<volatile unsigned int*>(g.seq);
+  const unsigned int* mine = g.flags[g.rank];
+  const uint64_t t0 = global_ns();
+#pragma unroll 1
+  for (int r = 0; r < g.world; ++r) {
+    for (uint32_t it = 0;; ++it) {
+      if (static_cast<int>(ld_acquire_sys_u32(mine + r) - s) >= 0) break;
+      if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+        record_error(kSiteGather);
+        return false;
+      }
+    }
+  }
+  return true;
 }
 
 // Host: launch with programmatic stream serialization (the kernel pairs it with

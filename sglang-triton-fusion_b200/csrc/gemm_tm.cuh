@@ -111,6 +111,7 @@ struct TmParams {
   float* partials;          // [G][2][MT][128]
   uint8_t* xq_out;          // optional [M, K]
   float* sx_out;            // optional [M, K/128]
+  GatherParams gather;      // N-sharded output written to every rank (world > 0)
 };
 
 // Shared memory, from the 1 KB-aligned base:
@@ -360,7 +361,8 @@ __device__ __forceinline__ void tm_touch_params(const TmParams& p) {
                reinterpret_cast<uint64_t>(p.counters) ^ reinterpret_cast<uint64_t>(p.partials) ^
                reinterpret_cast<uint64_t>(p.xq_out) ^ reinterpret_cast<uint64_t>(p.sx_out);
   uint32_t u = static_cast<uint32_t>(p.M ^ p.sw ^ p.lg_sw ^ p.kpb ^ p.nacc ^ p.stages ^ p.npw ^ p.N ^ p.K ^ p.KB ^
-                                     p.resident ^ p.csize ^ p.early_weights) ^
+                                     p.resident ^ p.csize ^ p.early_weights ^ p.gather.world ^
+                                     p.gather.wait_input) ^
                p.b_off ^ p.x_off ^ p.bar_off ^ p.x_tile_bytes;
   asm volatile("" ::"l"(t), "r"(u));
 }
@@ -396,7 +398,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // sx ring (a plain shared-memory flag; the epilogue polls it)
   volatile uint32_t* sx_tag = reinterpret_cast<volatile uint32_t*>(tmem_empty + kTmMaxAcc);
   uint64_t* drain = tmem_empty + kTmMaxAcc + kTmSxRing;  // MMA completion on the error path
-  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag
+  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag, [2] input wait failed
   // streaming: [kTmSxRing][MT] ring indexed by j; resident: [slot][M]
   float* sx_ring = reinterpret_cast<float*>(misc + 4);
   float* ws_cache = sx_ring + kTmSxRing * MT;          // [min(J, kTmWsCache)]
@@ -422,6 +424,13 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // divisions, done before the grid-dependency wait
   const int nb0 = static_cast<int>(u0 / p.KB);
   const int kb0 = static_cast<int>(u0 - static_cast<int64_t>(nb0) * p.KB);
+  // output element (token m, column n of this launch): local, or to every rank
+  auto store_out = [&](int m, int n, __nv_bfloat16 v) {
+    if (p.gather.world > 0)
+      gather_store(p.gather, m, n, v);
+    else
+      p.out[static_cast<int64_t>(m) * p.ldo + n] = v;
+  };
 
   if (warp == 0) {
     if (lane == 0) {
@@ -437,7 +446,10 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       mbar_init(&acc_full[lane], 1);     // tcgen05.commit
       mbar_init(&tmem_empty[lane], 4);   // 4 epilogue warps
     }
-    if (lane == 0) mbar_init(drain, 1);
+    if (lane == 0) {
+      mbar_init(drain, 1);
+      misc[2] = 0u;
+    }
     for (int r = lane; r < kTmSxRing; r += 32) sx_tag[r] = 0u;
     fence_mbar_init();
   } else if (warp == 1) {
@@ -481,6 +493,12 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   }
   grid_dependency_wait();
+  if (p.gather.wait_input) {
+    // the activation is a gathered output: every rank's slice must be here
+    if (tid == 0 && !gather_wait_input(p.gather)) misc[2] = 1u;
+    __syncthreads();
+    if (misc[2]) ok = false;
+  }
   // Warps 0 and 1 start their loops at once; warps 2-9 first finish the block
   // scales and, resident, quantise the CTA's K range (8 warps x 4 lane octets,
   // one 128-wide group per octet and pass), then meet at barrier 1.
@@ -853,7 +871,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         if (whole) {
 #pragma unroll
           for (int m = 0; m < MT; ++m)
-            if (m < p.M) p.out[static_cast<int64_t>(m) * p.ldo + n] = __float2bfloat16_rn(acc[m]);
+            if (m < p.M) store_out(m, n, __float2bfloat16_rn(acc[m]));
         } else if (p.csize > 1) {
           // cluster split-K: the partial sums stay in this CTA's shared memory
           // (the A tiles are free: every MMA has completed) and are reduced
@@ -898,7 +916,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             }
 #pragma unroll
             for (int m = 0; m < MT; ++m)
-              if (m < p.M) p.out[static_cast<int64_t>(m) * p.ldo + n] = __float2bfloat16_rn(sum[m]);
+              if (m < p.M) store_out(m, n, __float2bfloat16_rn(sum[m]));
           }
           named_bar_sync(2, 128);
         }
@@ -922,7 +940,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
         for (int q = 0; q < kTmMaxCluster; ++q)
           if (q < p.csize) sum += ld_dsmem(dsmem_addr(part + e, q));
-        p.out[static_cast<int64_t>(e >> 7) * p.ldo + nbc * 128 + (e & 127)] = __float2bfloat16_rn(sum);
+        store_out(e >> 7, nbc * 128 + (e & 127), __float2bfloat16_rn(sum));
       }
     }
     cluster_sync_all();   // this CTA's shared memory stays until the cluster has read it
@@ -930,6 +948,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
+  if (p.gather.world > 0 && tid == 0) gather_cta_done(p.gather, gridDim.x);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -1100,7 +1119,7 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
                      int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
                      float* sx_out, void* workspace, size_t workspace_bytes, int sm_count, int max_smem,
                      cudaStream_t stream, int early_weights = 0, int grid_override = 0,
-                     int resident_mode = 1, int cluster_mode = 1) {
+                     int resident_mode = 1, int cluster_mode = 1, const GatherParams* gather = nullptr) {
   const int MT = tm_token_tile(M);
   if (N / kGroup > kTmMaxRowBlocks) return 8;  // FP8GQ_ERR_UNSUPPORTED
   const size_t need = tm_workspace_bytes_for(M, N, K, sm_count);
@@ -1147,6 +1166,12 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     p.x = xp;
     p.ldx = ldx;
     p.early_weights = early_weights;
+    p.gather = gather ? *gather : GatherParams{};
+    if (gather) {
+      // this pass's rows of every rank's output; only the first pass waits
+      for (int r = 0; r < gather->world; ++r) p.gather.out[r] = gather->out[r] + static_cast<int64_t>(m0) * gather->ldo;
+      if (m0 > 0) p.gather.wait_input = 0;
+    }
     p.xq_out = xq_out ? xq_out + static_cast<int64_t>(m0) * K : nullptr;
     p.sx_out = sx_out ? sx_out + static_cast<int64_t>(m0) * (K / kGroup) : nullptr;
     CUtensorMap tmap_x;

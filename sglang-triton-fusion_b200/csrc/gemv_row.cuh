@@ -40,6 +40,7 @@ struct RowParams {
   uint8_t* xq_out;          // optional [K]
   float* sx_out;            // optional [K/128]
   int early_weights;        // weights are static: fetch the first stages before the grid-dependency wait
+  GatherParams gather;      // N-sharded output written to every rank (world > 0)
 };
 
 constexpr int kRowMaxConsumerThreads = 384;  // the launcher never picks T > 384
@@ -185,6 +186,14 @@ gemv_row_kernel(const RowParams p) {
   }
   // the activation and the output belong to the stream's previous work
   grid_dependency_wait();
+  bool in_ok = true;
+  if (p.gather.wait_input) {
+    // the activation is a gathered output: every rank's slice must be here
+    if (tid == 0) window[0] = gather_wait_input(p.gather) ? 1.0f : 0.0f;
+    named_bar_sync(1, T);
+    in_ok = window[0] != 0.0f;
+    named_bar_sync(1, T);
+  }
 
   // ------------------------------------------------- consumers: prologue --
   // Quantise this thread's chunks of the activation (whole 128-groups are
@@ -307,13 +316,22 @@ gemv_row_kernel(const RowParams p) {
         if (lane < nrows) {
           float sum = 0.0f;
           for (int w = 0; w < n_cwarps; ++w) sum += win[w * kRowWindow + lane];
-          p.out[row_begin + wrow0 + lane] = __float2bfloat16_rn(sum);
+          const __nv_bfloat16 v = __float2bfloat16_rn(sum);
+          if (p.gather.world > 0)
+            gather_store(p.gather, 0, row_begin + wrow0 + lane, v);
+          else
+            p.out[row_begin + wrow0 + lane] = v;
         }
       }
       win_buf ^= 1;
     }
   }
   (void)rows_my;
+  (void)in_ok;
+  if (p.gather.world > 0) {
+    named_bar_sync(1, T);   // every output store of this CTA is issued
+    if (tid == 0) gather_cta_done(p.gather, gridDim.x);
+  }
 }
 
 }  // namespace fp8gq

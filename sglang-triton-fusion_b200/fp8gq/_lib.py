@@ -27,6 +27,22 @@ STATUS = {
     10: "FP8GQ_ERR_SCRATCH_LIMIT",
 }
 
+MAX_GATHER_RANKS = 8   # FP8GQ_MAX_GATHER_RANKS
+
+
+class Gather(ctypes.Structure):
+    """struct fp8gq_gather (include/fp8gq.h)."""
+    _fields_ = [("out", ctypes.c_void_p * MAX_GATHER_RANKS),
+                ("flags", ctypes.c_void_p * MAX_GATHER_RANKS),
+                ("counter", ctypes.c_void_p),
+                ("seq", ctypes.c_void_p),
+                ("ldo", ctypes.c_int64),
+                ("col0", ctypes.c_int),
+                ("world", ctypes.c_int),
+                ("rank", ctypes.c_int),
+                ("wait_input", ctypes.c_int)]
+
+
 # name -> (restype, argtypes); the order of include/fp8gq.h
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -43,6 +59,12 @@ SIGNATURES = {
     "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "fp8gq_fused_gemv_quant_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
+                                           _P, _SZ, _P]),
+    "fp8gq_gather_wait": (_I, [ctypes.POINTER(Gather), _P]),
+    "fp8gq_ipc_get": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
+    "fp8gq_ipc_open": (_I, [_P, ctypes.c_uint64, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
+    "fp8gq_ipc_close": (_I, [_P]),
     "fp8gq_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _P]),
     "fp8gq_swiglu_quant": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _P]),
     "fp8gq_set_static_weights": (_I, [_I]),

@@ -3,15 +3,24 @@
 The output columns of a linear are independent, so rank r of `world` holds
 rows [r*N/world, (r+1)*N/world) of the weight (whole 128-row blocks, so the
 block scales split with it), runs the fused op on that slice and the bf16
-slices are all-gathered (NCCL on GPUs).  The activation is replicated;
-every rank quantises it itself.
+slices are gathered on every rank.  The activation is replicated; every rank
+quantises it itself.
+
+Two ways to gather:
+  * all_gather_columns / gathered_linear: the op, then an all-gather (NCCL on
+    GPUs, gloo on CPU);
+  * PeerGather: the kernel itself stores its slice into every rank's output
+    buffer over NVLink (peer memory mapped with CUDA IPC) and raises a flag;
+    the next gathered call waits for the flags inside its kernel.
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 
-from . import ops
+from . import _lib, ops
 
 
 def shard_rows(Wq: torch.Tensor, Ws: torch.Tensor, rank: int, world: int):
@@ -50,3 +59,106 @@ def gathered_linear(x: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Ten
     (M, N) output on every rank.  `op` defaults to fp8gq.fused_gemv_quant."""
     op = op or ops.fused_gemv_quant
     return all_gather_columns(op(x, Wq_shard, Ws_shard), group=group)
+
+
+class PeerGather:
+    """Gathered linears over peer memory (fp8gq_fused_gemv_quant_gather).
+
+    ``buffer`` is this rank's storage for full outputs: the same size, dtype
+    bf16, on every rank.  It and a small flag array are mapped into every
+    other rank (CUDA IPC, exchanged through ``group``).  ``linear`` writes the
+    output of this rank's weight rows into columns ``col0 ..`` of ``out`` -- a
+    [M, N] view into ``buffer`` -- on every rank at once.  Every rank must make
+    the same sequence of ``linear`` calls.  ``wait()`` enqueues a wait for the
+    last call's slices from every rank (before anything else reads ``out``).
+    """
+
+    def __init__(self, buffer: torch.Tensor, group=None):
+        if buffer.dtype != torch.bfloat16 or not buffer.is_cuda or not buffer.is_contiguous():
+            raise TypeError("buffer must be a contiguous CUDA bf16 tensor")
+        self.lib = _lib.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= _lib.MAX_GATHER_RANKS:
+            raise ValueError(f"PeerGather needs 2..{_lib.MAX_GATHER_RANKS} ranks, got {self.world}")
+        self.buffer = buffer
+        dev = buffer.device
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=dev)
+        self.state = torch.zeros(2, dtype=torch.int32, device=dev)        # counter, seq
+        mine = (self._handle(buffer.data_ptr()), self._handle(self.flags.data_ptr()))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=group)
+        self._bases = []
+        self.buf_ptrs, self.flag_ptrs = [], []
+        for r, (hb, hf) in enumerate(allh):
+            if r == self.rank:
+                self.buf_ptrs.append(buffer.data_ptr())
+                self.flag_ptrs.append(self.flags.data_ptr())
+            else:
+                self.buf_ptrs.append(self._open(hb))
+                self.flag_ptrs.append(self._open(hf))
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def _handle(self, ptr):
+        h = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _lib.check(self.lib.fp8gq_ipc_get(ptr, h, ctypes.byref(off)), "fp8gq_ipc_get")
+        return bytes(h.raw), int(off.value)
+
+    def _open(self, hoff):
+        h, off = hoff
+        base, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+        _lib.check(self.lib.fp8gq_ipc_open(ctypes.create_string_buffer(h, 64), off, ctypes.byref(base),
+                                           ctypes.byref(ptr)), "fp8gq_ipc_open")
+        self._bases.append(base.value)
+        return ptr.value
+
+    def descriptor(self, out: torch.Tensor, col0: int, wait_input: bool) -> "_lib.Gather":
+        """The struct fp8gq_gather for output view ``out`` of ``buffer``."""
+        off = out.data_ptr() - self.buffer.data_ptr()
+        if off < 0 or off + out.numel() * 2 > self.buffer.numel() * 2 or out.stride(1) != 1:
+            raise ValueError("out must be a row-major view into the PeerGather buffer")
+        g = _lib.Gather()
+        for r in range(self.world):
+            g.out[r] = self.buf_ptrs[r] + off
+            g.flags[r] = self.flag_ptrs[r]
+        g.counter = self.state.data_ptr()
+        g.seq = self.state.data_ptr() + 4
+        g.ldo = out.stride(0)
+        g.col0 = col0
+        g.world = self.world
+        g.rank = self.rank
+        g.wait_input = 1 if wait_input else 0
+        return g
+
+    def linear(self, x: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Tensor, out: torch.Tensor,
+               wait_input: bool = True, desc=None):
+        """out[:, rank*Nr:(rank+1)*Nr] = fused_gemv_quant(x, Wq_shard, Ws_shard) on every rank."""
+        M, K = x.shape
+        Nr = Wq_shard.shape[0]
+        ops._check_weight(Wq_shard, Ws_shard, K)
+        if out.shape != (M, Nr * self.world):
+            raise ops.ShapeError(f"out must be [{M}, {Nr * self.world}], got {tuple(out.shape)}")
+        g = desc if desc is not None else self.descriptor(out, self.rank * Nr, wait_input)
+        nbytes = self.lib.fp8gq_workspace_bytes(M, Nr, K)
+        ws_buf = ops.workspace(x.device, nbytes) if nbytes else None
+        st = self.lib.fp8gq_fused_gemv_quant_gather(
+            x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), Wq_shard.stride(0), Ws_shard.data_ptr(),
+            Ws_shard.stride(0), M, Nr, K, ctypes.byref(g), None if ws_buf is None else ws_buf.data_ptr(),
+            0 if ws_buf is None else ws_buf.numel(), ops._stream(x.device))
+        _lib.check(st, "fp8gq_fused_gemv_quant_gather")
+        return out
+
+    def wait(self, out: torch.Tensor):
+        """Enqueue a wait for the last gathered call's slices from every rank."""
+        g = self.descriptor(out, 0, True)
+        _lib.check(self.lib.fp8gq_gather_wait(ctypes.byref(g), ops._stream(out.device)), "fp8gq_gather_wait")
+
+    def close(self):
+        torch.cuda.synchronize(self.buffer.device)
+        dist.barrier(group=self.group)
+        for b in self._bases:
+            self.lib.fp8gq_ipc_close(b)
+        self._bases = []

@@ -287,6 +287,23 @@ def test_swiglu_down_proj(fp8gq, cuda_device, M):
     assert_close(to_f32(out), exact, 3.0)
 
 
+# ------------------------------------------------------------- lm_head --
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_lm_head_vocab_rows(fp8gq, cuda_device, M):
+    """lm_head-shaped GEMV: N = 151936 vocabulary rows (1187 row blocks, a
+    stream-K grid with CTA ranges crossing row blocks); K cut to 1024 so the
+    float64 oracle stays quick.  kernels/fused_gemv_quant.py:82 and
+    kernels/fused_gemv_quant_tm.py:123 bench this shape."""
+    K, N = 1024, 151936
+    x = gpu_activation(M, K, 400 + M, cuda_device)
+    wq, ws = gpu_weight(N, K, 401, cuda_device)
+    out, xq, sx = fp8gq.fused_gemv_quant(x, wq, ws, return_quant=True)
+    _, exact, rq, rs = oracle_of(x, wq, ws)
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert_close(to_f32(out), exact, 3.0)
+
+
 # ---------------------------------------- stand-alone SwiGLU writers --
 
 @pytest.mark.parametrize("M, I", [(512, 9728), (16, 9728), (3, 256), (1, 12288)])
