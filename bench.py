@@ -406,6 +406,26 @@ def run_ours(args):
                 tmb[f"{name}_M{M}"] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1)}
             del wl
         extra["tm_blocked_qwen3_4b"] = tmb
+        # add + RMSNorm as the prologue of qkv and gate_up (M = 1), against the
+        # norm as its own kernel followed by the linear
+        nrm = {}
+        hid = torch.randn(1, 4096, device=dev).bfloat16()
+        resid = torch.randn(1, 4096, device=dev).bfloat16()
+        nw = (torch.randn(4096, device=dev) * 0.1 + 1).bfloat16()
+        hbuf = torch.empty(1, 4096, dtype=torch.bfloat16, device=dev)
+        rbuf = torch.empty(1, 4096, dtype=torch.bfloat16, device=dev)
+        for i, name in ((0, "qkv"), (2, "gate_up")):
+            outs_ = [lin[i][6] for lin in layers]
+            fused = [lambda lin=lin, o=o: fp8gq.fused_add_rmsnorm_gemv_quant(hid, resid, nw, lin[i][3], lin[i][4],
+                                                                            out=o, residual_out=rbuf)
+                     for lin, o in zip(layers, outs_)]
+
+            def unfused_call(lin, o):
+                fp8gq.add_rmsnorm(hid, resid, nw, out=hbuf, residual_out=rbuf)
+                fp8gq.fused_gemv_quant(hbuf, lin[i][3], lin[i][4], out=o)
+            unfused = [lambda lin=lin, o=o: unfused_call(lin, o) for lin, o in zip(layers, outs_)]
+            nrm[name] = {"fused_us": round(graph_us(fused), 3), "norm_then_linear_us": round(graph_us(unfused), 3)}
+        extra["add_rmsnorm_prologue_m1"] = nrm
         # lm_head of Qwen3-8B (151936 x 4096, 622 MB of e4m3), two weight copies
         lm = [make_weight_gpu(151936, 4096, seed=900 + c, dev=dev) for c in range(2)]
         lmh = {}

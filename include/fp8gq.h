@@ -173,6 +173,35 @@ int fp8gq_ipc_get(const void *ptr, void *handle64, uint64_t *offset);
 int fp8gq_ipc_open(const void *handle64, uint64_t offset, void **base, void **ptr);
 int fp8gq_ipc_close(void *base);
 
+/* Fused add + RMSNorm (the reference's add_rmsnorm_kernel,
+ * kernels/fused_rmsnorm.py:14-27), bf16 x, residual [M, K] and norm weight
+ * [K], K % 128 == 0, 16-byte aligned rows:
+ *   s = x + residual (fp32);  residual_out = bf16(s)
+ *   rstd = 1 / sqrt(sum(s^2) / K + eps)   (IEEE sqrt and division; the sum in a
+ *          fixed order: 16-value chunks left to right, the 8 chunks of a
+ *          128-group pairwise, the groups left to right)
+ *   out = bf16((s * rstd) * w)
+ * residual_out may be NULL (not written). */
+int fp8gq_add_rmsnorm(const void *x, int64_t ldx, const void *residual, int64_t ldr, const void *norm_w,
+                      float eps, void *out, int64_t ldo, void *residual_out, int64_t ldro, int M, int K,
+                      fp8gq_stream_t stream);
+
+/* The same add + RMSNorm as the prologue of the fused quant + GEMV: out =
+ * GEMV(quant(norm output)) with the norm output never stored -- the norm's
+ * launch leaves the decode chain.  Bit-identical to fp8gq_add_rmsnorm followed
+ * by fp8gq_fused_gemv_quant on its output.  residual_out (may be NULL) must
+ * not overlap residual (other CTAs still read it while it is written).
+ * Routing and workspace as fp8gq_fused_gemv_quant; the tile kernel needs its
+ * resident activation feed here and returns FP8GQ_ERR_UNSUPPORTED for shapes
+ * where that does not fit.  No counterpart in the reference (it runs the norm
+ * as its own kernel). */
+int fp8gq_fused_add_rmsnorm_gemv_quant(const void *x, int64_t ldx, const void *residual, int64_t ldr,
+                                       const void *norm_w, float eps, const void *w, int64_t ldw,
+                                       const float *ws, int64_t ldws, void *out, int64_t ldo,
+                                       void *residual_out, int64_t ldro, int M, int N, int K,
+                                       uint8_t *xq_out, float *sx_out, void *workspace, size_t workspace_bytes,
+                                       fp8gq_stream_t stream);
+
 /* Stand-alone SwiGLU writers for any M (the prefill side, M > 16), gate and up
  * as separate bf16 [M, I] operands (row strides ldg, ldu elements, 16-byte
  * aligned), I % 128 == 0:

@@ -298,6 +298,62 @@ def fused_swiglu_q_gemm(gu: np.ndarray, wq: np.ndarray, ws: np.ndarray):
 
 
 # --------------------------------------------------------------------------
+# add + RMSNorm prologue (kernels/fused_rmsnorm.py:14-27, decode dtypes)
+# --------------------------------------------------------------------------
+
+RMS_EPS = np.float32(1e-6)
+
+
+def add_rmsnorm(x: np.ndarray, r: np.ndarray, w: np.ndarray, eps=RMS_EPS):
+    """Fused add + RMSNorm as the kernels evaluate it, every step one rounded
+    fp32 operation (no fused multiply-add), so the CUDA kernels match bit for
+    bit.  The reference kernel (kernels/fused_rmsnorm.py:14-27) computes
+        s = x + r;  residual_out = s;  rstd = rsqrt(mean(s^2) + eps);
+        out = s * rstd * w
+    Here x, r are bf16 [M, K] (float32 values), w the bf16 norm weight [K]:
+      s     = f32(x) + f32(r)                    residual_out = bf16(s)
+      ssq   = sum of s^2 in a fixed order: per 16-element chunk left to right,
+              the 8 chunks of a 128-group pairwise ((c0+c1)+(c2+c3)) +
+              ((c4+c5)+(c6+c7)), the K/128 group sums left to right
+      rstd  = 1 / sqrt(ssq / K + eps)            (IEEE division and sqrt)
+      out   = bf16((s * rstd) * w)
+    Returns (out, residual_out, rstd) as float32 arrays ([M, K], [M, K], [M])."""
+    x = np.asarray(x, np.float32)
+    r = np.asarray(r, np.float32)
+    w = np.asarray(w, np.float32)
+    M, K = x.shape
+    if K % GROUP:
+        raise ValueError("K must be a multiple of 128")
+    s = (x + r).astype(np.float32)
+    sq = (s * s).astype(np.float32).reshape(M, K // GROUP, 8, 16)
+    c = np.zeros(sq.shape[:3], np.float32)
+    for k in range(16):                                            # chunk sums, left to right
+        c = (c + sq[..., k]).astype(np.float32)
+    p01 = (c[..., 0] + c[..., 1]).astype(np.float32)
+    p23 = (c[..., 2] + c[..., 3]).astype(np.float32)
+    p45 = (c[..., 4] + c[..., 5]).astype(np.float32)
+    p67 = (c[..., 6] + c[..., 7]).astype(np.float32)
+    g = ((p01 + p23).astype(np.float32) + (p45 + p67).astype(np.float32)).astype(np.float32)
+    ssq = np.zeros(M, np.float32)
+    for b in range(K // GROUP):                                    # group sums, left to right
+        ssq = (ssq + g[:, b]).astype(np.float32)
+    var = (ssq / np.float32(K)).astype(np.float32)
+    rstd = (np.float32(1.0) / np.sqrt((var + np.float32(eps)).astype(np.float32))).astype(np.float32)
+    h = ((s * rstd[:, None]).astype(np.float32) * w[None, :]).astype(np.float32)
+    return bf16_round(h), bf16_round(s), rstd
+
+
+def fused_add_rmsnorm_gemv_quant(x, r, nw, wq, ws, eps=RMS_EPS):
+    """The GEMV fed by the add + RMSNorm prologue: quantises the bf16 norm
+    output exactly as fused_gemv_quant quantises its input.  Returns
+    (out_bf16_as_f32, exact_f64, xq, sx, residual_out)."""
+    h, res, _ = add_rmsnorm(x, r, nw, eps)
+    xq, sx = group_quant(h)
+    exact = gemv_from_quant(xq, sx, wq, ws)
+    return bf16_round(exact.astype(np.float32)), exact, xq, sx, res
+
+
+# --------------------------------------------------------------------------
 # tolerances used by the reference's own self-tests
 # --------------------------------------------------------------------------
 

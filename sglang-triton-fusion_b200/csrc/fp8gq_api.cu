@@ -13,6 +13,7 @@
 #include "gemv_row.cuh"
 #include "quant_only.cuh"
 #include "swiglu_writer.cuh"
+#include "add_rmsnorm.cuh"
 
 using namespace fp8gq;
 
@@ -107,7 +108,7 @@ constexpr int kRowRingBytes = 96 * 1024;    // per CTA; two CTAs per SM
 
 int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const float* ws, int64_t ldws,
                void* out, int N, int K, uint8_t* xq_out, float* sx_out, cudaStream_t stream,
-               const GatherParams* gather = nullptr) {
+               const GatherParams* gather = nullptr, const NormParams* norm = nullptr) {
   DeviceInfo di;
   int dev = 0;
   int st = device_info(&di, &dev);
@@ -148,6 +149,7 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   p.xq_out = xq_out;
   p.sx_out = sx_out;
   p.gather = gather ? *gather : GatherParams{};
+  p.norm = norm ? *norm : NormParams{};
   p.early_weights = g_static_weights.load(std::memory_order_relaxed);
   int grid = 2 * di.sm_count;
   if (grid > p.n_groups) grid = p.n_groups;
@@ -359,6 +361,70 @@ int fp8gq_swiglu_group_quant(const void* gu, int64_t ldgu, int M, int I, uint8_t
       (reinterpret_cast<uintptr_t>(sx) & 3u))
     return FP8GQ_ERR_ALIGNMENT;
   return launch_quant(true, gu, ldgu, M, I, xq, sx, static_cast<cudaStream_t>(stream));
+}
+
+int fp8gq_add_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t ldr, const void* norm_w,
+                      float eps, void* out, int64_t ldo, void* residual_out, int64_t ldro, int M, int K,
+                      fp8gq_stream_t stream) {
+  if (!x || !residual || !norm_w || !out) return FP8GQ_ERR_NULL_POINTER;
+  if (M < 1 || K <= 0 || K % kGroup) return FP8GQ_ERR_SHAPE;
+  if (ldx < K || ldr < K || ldo < K || (residual_out && ldro < K)) return FP8GQ_ERR_STRIDE;
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(residual) |
+                        reinterpret_cast<uintptr_t>(norm_w) | reinterpret_cast<uintptr_t>(out) |
+                        reinterpret_cast<uintptr_t>(residual_out);
+  if ((mis & 15u) || (ldx % 8) || (ldr % 8) || (ldo % 8) || (residual_out && (ldro % 8))) return FP8GQ_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  const size_t smem = static_cast<size_t>(K / kGroup + 1) * sizeof(float);
+  if (smem > static_cast<size_t>(di.max_smem_optin)) return FP8GQ_ERR_UNSUPPORTED;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(add_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  if (launch_with_pdl(add_rmsnorm_kernel, dim3(M), dim3(kNormThreads), smem, static_cast<cudaStream_t>(stream),
+                      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(residual), ldr,
+                      static_cast<const __nv_bfloat16*>(norm_w), eps, static_cast<__nv_bfloat16*>(out), ldo,
+                      static_cast<__nv_bfloat16*>(residual_out), ldro, K) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  return launch_status();
+}
+
+int fp8gq_fused_add_rmsnorm_gemv_quant(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                                       const void* norm_w, float eps, const void* w, int64_t ldw, const float* ws,
+                                       int64_t ldws, void* out, int64_t ldo, void* residual_out, int64_t ldro,
+                                       int M, int N, int K, uint8_t* xq_out, float* sx_out, void* workspace,
+                                       size_t workspace_bytes, fp8gq_stream_t stream) {
+  int st = check_common(x, w, ws, out, M, N, K, ldw, ldws, ldo);
+  if (st != FP8GQ_OK) return st;
+  if (!residual || !norm_w) return FP8GQ_ERR_NULL_POINTER;
+  if (ldx < K || ldr < K || (residual_out && ldro < K)) return FP8GQ_ERR_STRIDE;
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(norm_w) |
+                        reinterpret_cast<uintptr_t>(residual_out);
+  if ((mis & 15u) || (ldx % 8) || (ldr % 8) || (residual_out && (ldro % 8))) return FP8GQ_ERR_ALIGNMENT;
+  if (residual_out) {
+    // CTA 0 writes residual_out while other CTAs still read residual
+    const uintptr_t r0 = reinterpret_cast<uintptr_t>(residual), o0 = reinterpret_cast<uintptr_t>(residual_out);
+    const uintptr_t r1 = r0 + static_cast<uintptr_t>((static_cast<int64_t>(M - 1) * ldr + K) * 2);
+    const uintptr_t o1 = o0 + static_cast<uintptr_t>((static_cast<int64_t>(M - 1) * ldro + K) * 2);
+    if (r0 < o1 && o0 < r1) return FP8GQ_ERR_UNSUPPORTED;
+  }
+  NormParams nrm{};
+  nrm.res = static_cast<const __nv_bfloat16*>(residual);
+  nrm.w = static_cast<const __nv_bfloat16*>(norm_w);
+  nrm.res_out = static_cast<__nv_bfloat16*>(residual_out);
+  nrm.ldr = ldr;
+  nrm.ldro = ldro;
+  nrm.eps = eps;
+  nrm.norm = 1;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 1 && m1_uses_row(N, K)) return launch_row(false, x, w, ldw, ws, ldws, out, N, K, xq_out, sx_out, s, nullptr, &nrm);
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace, workspace_bytes,
+                   di.sm_count, di.max_smem_optin, s, g_static_weights.load(std::memory_order_relaxed), 0,
+                   1, tm_cluster_mode(), nullptr, &nrm);
 }
 
 int fp8gq_fused_gemv_quant_gather(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,

@@ -217,6 +217,78 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
 }
 
 // ---------------------------------------------------------------------------
+// add + RMSNorm prologue (kernels/fused_rmsnorm.py:14-27): s = x + r in fp32,
+// rstd = 1 / sqrt(mean(s^2) + eps), out = bf16((s * rstd) * w).  The sum of
+// squares has a fixed order -- per 16-value chunk left to right, the 8
+// chunks of a 128-group pairwise, the groups left to right -- and every step
+// is one rounded fp32 operation, so the CPU oracle reproduces it bit for bit.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float sumsq16(const float (&v)[16]) {
+  float a = 0.0f;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) a = __fadd_rn(a, __fmul_rn(v[e], v[e]));
+  return a;
+}
+
+// Sum over a lane octet (8 consecutive lanes): ((c0+c1)+(c2+c3))+((c4+c5)+(c6+c7)),
+// the same bits on every lane of the octet.  All 32 lanes call it together.
+__device__ __forceinline__ float octet_sum(float c) {
+  c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 1));
+  c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 2));
+  c = __fadd_rn(c, __shfl_xor_sync(0xffffffffu, c, 4));
+  return c;
+}
+
+__device__ __forceinline__ float rms_rstd(float ssq, int K, float eps) {
+  const float var = __fdiv_rn(ssq, static_cast<float>(K));
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+}
+
+// 16 values s = x + r from two 16-byte words of bf16 each.
+__device__ __forceinline__ void add16(float (&s)[16], uint4 xa, uint4 xb, uint4 ra, uint4 rb) {
+  const uint32_t xw[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+  const uint32_t rw[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    s[2 * e] = __fadd_rn(bf16_lo(xw[e]), bf16_lo(rw[e]));
+    s[2 * e + 1] = __fadd_rn(bf16_hi(xw[e]), bf16_hi(rw[e]));
+  }
+}
+
+// Norm output bf16((s * rstd) * w) for 16 values (w: two 16-byte words of
+// bf16), returned as the float values of the bf16 results.
+__device__ __forceinline__ void norm16(float (&h)[16], const float (&s)[16], float rstd, uint4 wa, uint4 wb) {
+  const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    h[2 * e] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s[2 * e], rstd), bf16_lo(ww[e]))));
+    h[2 * e + 1] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s[2 * e + 1], rstd), bf16_hi(ww[e]))));
+  }
+}
+
+// 16 bf16 values (round to nearest even) packed into two 16-byte words.
+__device__ __forceinline__ void pack_bf16x16(const float (&s)[16], uint4& a, uint4& b) {
+  uint32_t w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(s[2 * e], s[2 * e + 1]);
+    w[e] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  a = make_uint4(w[0], w[1], w[2], w[3]);
+  b = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// Parameters of the add + RMSNorm prologue (norm = 0: none).
+struct NormParams {
+  const __nv_bfloat16* res;   // residual [M, ldr]
+  const __nv_bfloat16* w;     // norm weight [K]
+  __nv_bfloat16* res_out;     // x + residual [M, ldro], written once (by CTA 0)
+  int64_t ldr, ldro;
+  float eps;
+  int norm;
+};
+
+// ---------------------------------------------------------------------------
 // N-sharded output gather over peer memory (one process per GPU, NVLink)
 // ---------------------------------------------------------------------------
 constexpr int kMaxGatherRanks = 8;

@@ -112,13 +112,14 @@ struct TmParams {
   uint8_t* xq_out;          // optional [M, K]
   float* sx_out;            // optional [M, K/128]
   GatherParams gather;      // N-sharded output written to every rank (world > 0)
+  NormParams norm;          // add + RMSNorm prologue (resident activation only)
 };
 
 // Shared memory, from the 1 KB-aligned base:
 //   A tiles [S][16 KB] | B tiles [S][MT x 128 B] | activation region (streaming:
 //   [S] bf16 tiles; resident: xq of the K range) | full[8] xfull[8] empty[8]
 //   acc_full[ACC] tmem_empty[ACC] sx_tag[SXR] (8 B each) drain | misc[4] |
-//   sx ring (resident: sx of the K range) | ws cache
+//   sx ring (resident: sx of the K range) | ws cache | add + RMSNorm sums
 // In cluster mode the A-tile area holds the CTA's split-K partial sums once
 // its MMAs are done.
 template <int MT, bool kSwiglu>
@@ -362,7 +363,7 @@ __device__ __forceinline__ void tm_touch_params(const TmParams& p) {
                reinterpret_cast<uint64_t>(p.xq_out) ^ reinterpret_cast<uint64_t>(p.sx_out);
   uint32_t u = static_cast<uint32_t>(p.M ^ p.sw ^ p.lg_sw ^ p.kpb ^ p.nacc ^ p.stages ^ p.npw ^ p.N ^ p.K ^ p.KB ^
                                      p.resident ^ p.csize ^ p.early_weights ^ p.gather.world ^
-                                     p.gather.wait_input) ^
+                                     p.gather.wait_input ^ p.norm.norm) ^
                p.b_off ^ p.x_off ^ p.bar_off ^ p.x_tile_bytes;
   asm volatile("" ::"l"(t), "r"(u));
 }
@@ -402,6 +403,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // streaming: [kTmSxRing][MT] ring indexed by j; resident: [slot][M]
   float* sx_ring = reinterpret_cast<float*>(misc + 4);
   float* ws_cache = sx_ring + kTmSxRing * MT;          // [min(J, kTmWsCache)]
+  float* norm_sum = ws_cache + kTmWsCache;             // add + RMSNorm: [M][K/128] group sums, then rstd [M]
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -526,70 +528,138 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         kb = res_full ? r : kb0 + r;
         if (kb >= p.KB) kb -= p.KB;
       };
-      // The loads of kPasses passes are issued before any of them is
-      // quantised (L2-coherent loads: the activation may come from the kernel
-      // before this one in the stream), so a pass costs one L2 round trip per
-      // kPasses passes rather than one each.
-      constexpr int kPasses = kSwiglu ? 2 : 4;
-      constexpr int kWords = kSwiglu ? 4 : 2;
-      for (int g0 = 0; g0 < ngroups; g0 += 32 * kPasses) {
-        uint4 wd[kPasses][kWords];
+      // a quantised group: resident bytes and scale, the first ring's B
+      // tiles, the optional outputs
+      auto commit = [&](int m, int r, int kb, uint4 packed, float sx) {
+        *reinterpret_cast<uint4*>(x_tiles + (static_cast<int64_t>(r) * p.M + m) * 128 + chunk * 16) = packed;
+        if (chunk == 0) sx_ring[r * p.M + m] = sx;
+        // first-ring tiles j < nfirst that use slot r: j = r (slot = tile),
+        // or j = r - kb0 mod KB and every KB after it (slot = K block)
+        int jj = r;
+        int step = nfirst;
+        if (res_full) {
+          jj = r - kb0;
+          if (jj < 0) jj += p.KB;
+          step = p.KB;
+        }
+        for (; jj < nfirst; jj += step) {
+          const int br = tile_pos(jj, kb0, p.KB, kpb) * p.sw + m;
+          *reinterpret_cast<uint4*>(b_tiles + jj * Cfg::kBTileBytes + br * 128 + ((chunk ^ (br & 7)) << 4)) = packed;
+        }
+        if (kb >= u0 && kb < u1) {
+          // this CTA holds tile (row block 0, kb): it writes the optional outputs
+          if (p.xq_out)
+            *reinterpret_cast<uint4*>(p.xq_out + static_cast<int64_t>(m) * p.K + kb * 128 + chunk * 16) = packed;
+          if (p.sx_out && chunk == 0) p.sx_out[static_cast<int64_t>(m) * p.KB + kb] = sx;
+        }
+      };
+      if (!kSwiglu && p.norm.norm) {
+        // add + RMSNorm: every CTA first sums the squares of the whole rows
+        // (all K blocks, not only its own) -- chunk sums, octet sums per
+        // 128-group into norm_sum[m][b] -- and one thread per token adds the
+        // groups in order
+        float* gsum = norm_sum;
+        const int ng_all = p.M * p.KB;
+        for (int g0 = 0; g0 < ng_all; g0 += 32) {
+          const int g = g0 + oct;
+          const bool live = g < ng_all;
+          const int m = live ? g / p.KB : 0;
+          const int b = live ? g - m * p.KB : 0;
+          float sv[16];
+          if (live) {
+            const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + b * 128 + chunk * 16);
+            const uint4* rr =
+                reinterpret_cast<const uint4*>(p.norm.res + static_cast<int64_t>(m) * p.norm.ldr + b * 128 + chunk * 16);
+            add16(sv, __ldcg(xr), __ldcg(xr + 1), __ldcg(rr), __ldcg(rr + 1));
+          } else {
 #pragma unroll
-        for (int i = 0; i < kPasses; ++i) {
-          const int g = g0 + 32 * i + oct;
-          if (g < ngroups) {
-            int m, r, kb;
-            group_of(g, m, r, kb);
-            const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 +
-                                                             chunk * 16);
-            wd[i][0] = __ldcg(xr);
-            wd[i][1] = __ldcg(xr + 1);
-            if constexpr (kSwiglu) {
-              const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(xr) + p.K);
-              wd[i][kWords - 2] = __ldcg(ur);
-              wd[i][kWords - 1] = __ldcg(ur + 1);
-            }
+            for (int e = 0; e < 16; ++e) sv[e] = 0.0f;
+          }
+          const float gs = octet_sum(sumsq16(sv));
+          if (live && chunk == 0) gsum[m * p.KB + b] = gs;
+          if (live && blockIdx.x == 0 && p.norm.res_out) {
+            uint4 wa, wb;
+            pack_bf16x16(sv, wa, wb);
+            uint4* op =
+                reinterpret_cast<uint4*>(p.norm.res_out + static_cast<int64_t>(m) * p.norm.ldro + b * 128 + chunk * 16);
+            op[0] = wa;
+            op[1] = wb;
           }
         }
-#pragma unroll
-        for (int i = 0; i < kPasses; ++i) {
-          if (g0 + 32 * i >= ngroups) break;   // uniform across the warp
-          const int g = g0 + 32 * i + oct;
+        named_bar_sync(1, kTmThreads - 64);
+        if (tid - 64 < p.M) {
+          const int m = tid - 64;
+          float acc_s = 0.0f;
+          for (int b = 0; b < p.KB; ++b) acc_s = __fadd_rn(acc_s, gsum[m * p.KB + b]);
+          gsum[p.M * p.KB + m] = rms_rstd(acc_s, p.K, p.norm.eps);
+        }
+        named_bar_sync(1, kTmThreads - 64);
+        // then the CTA's own K blocks: the bf16 norm output, quantised
+        for (int g0 = 0; g0 < ngroups; g0 += 32) {
+          const int g = g0 + oct;
           const bool live = g < ngroups;
           int m = 0, r = 0, kb = 0;
           if (live) group_of(g, m, r, kb);
           float v[16];
           if (live) {
-            act16<kSwiglu>(v, wd[i][0], wd[i][1], wd[i][kWords - 2], wd[i][kWords - 1]);
+            const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 + chunk * 16);
+            const uint4* rr =
+                reinterpret_cast<const uint4*>(p.norm.res + static_cast<int64_t>(m) * p.norm.ldr + kb * 128 + chunk * 16);
+            const uint4* wr = reinterpret_cast<const uint4*>(p.norm.w + kb * 128 + chunk * 16);
+            float sv[16];
+            add16(sv, __ldcg(xr), __ldcg(xr + 1), __ldcg(rr), __ldcg(rr + 1));
+            norm16(v, sv, gsum[p.M * p.KB + m], __ldg(wr), __ldg(wr + 1));
           } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] = 0.0f;
           }
           float sx;
           const uint4 packed = quant16_octet(v, live, sx);
-          if (live) {
-            *reinterpret_cast<uint4*>(x_tiles + (static_cast<int64_t>(r) * p.M + m) * 128 + chunk * 16) = packed;
-            if (chunk == 0) sx_ring[r * p.M + m] = sx;
-            // first-ring tiles j < nfirst that use slot r: j = r (slot = tile),
-            // or j = r - kb0 mod KB and every KB after it (slot = K block)
-            int jj = r;
-            int step = nfirst;
-            if (res_full) {
-              jj = r - kb0;
-              if (jj < 0) jj += p.KB;
-              step = p.KB;
+          if (live) commit(m, r, kb, packed, sx);
+        }
+      } else {
+        // The loads of kPasses passes are issued before any of them is
+        // quantised (L2-coherent loads: the activation may come from the
+        // kernel before this one in the stream), so a pass costs one L2 round
+        // trip per kPasses passes rather than one each.
+        constexpr int kPasses = kSwiglu ? 2 : 4;
+        constexpr int kWords = kSwiglu ? 4 : 2;
+        for (int g0 = 0; g0 < ngroups; g0 += 32 * kPasses) {
+          uint4 wd[kPasses][kWords];
+#pragma unroll
+          for (int i = 0; i < kPasses; ++i) {
+            const int g = g0 + 32 * i + oct;
+            if (g < ngroups) {
+              int m, r, kb;
+              group_of(g, m, r, kb);
+              const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 +
+                                                               chunk * 16);
+              wd[i][0] = __ldcg(xr);
+              wd[i][1] = __ldcg(xr + 1);
+              if constexpr (kSwiglu) {
+                const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(xr) + p.K);
+                wd[i][kWords - 2] = __ldcg(ur);
+                wd[i][kWords - 1] = __ldcg(ur + 1);
+              }
             }
-            for (; jj < nfirst; jj += step) {
-              const int br = tile_pos(jj, kb0, p.KB, kpb) * p.sw + m;
-              *reinterpret_cast<uint4*>(b_tiles + jj * Cfg::kBTileBytes + br * 128 + ((chunk ^ (br & 7)) << 4)) =
-                  packed;
+          }
+#pragma unroll
+          for (int i = 0; i < kPasses; ++i) {
+            if (g0 + 32 * i >= ngroups) break;   // uniform across the warp
+            const int g = g0 + 32 * i + oct;
+            const bool live = g < ngroups;
+            int m = 0, r = 0, kb = 0;
+            if (live) group_of(g, m, r, kb);
+            float v[16];
+            if (live) {
+              act16<kSwiglu>(v, wd[i][0], wd[i][1], wd[i][kWords - 2], wd[i][kWords - 1]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[e] = 0.0f;
             }
-            if (kb >= u0 && kb < u1) {
-              // this CTA holds tile (row block 0, kb): it writes the optional outputs
-              if (p.xq_out)
-                *reinterpret_cast<uint4*>(p.xq_out + static_cast<int64_t>(m) * p.K + kb * 128 + chunk * 16) = packed;
-              if (p.sx_out && chunk == 0) p.sx_out[static_cast<int64_t>(m) * p.KB + kb] = sx;
-            }
+            float sx;
+            const uint4 packed = quant16_octet(v, live, sx);
+            if (live) commit(m, r, kb, packed, sx);
           }
         }
       }
@@ -1052,13 +1122,13 @@ struct TmPlan {
 // scales in the sx ring -- is used when it still leaves at least 4 stages.
 template <int MT, bool SW>
 inline bool tm_plan(TmPlan* pl, int M, int64_t U, int64_t KB, int grid, int sm_count, int max_smem,
-                    int resident_mode) {
+                    int resident_mode, int64_t extra_tail = 0) {
   using Cfg = TmCfg<MT, SW>;
   const bool one_per_sm = tm_ctas_per_sm<MT>() == 1 || grid <= sm_count;
   int64_t budget = one_per_sm ? max_smem
                               : static_cast<int64_t>(kTmSmemBudgetSm / tm_ctas_per_sm<MT>() - kTmSmemReservedPerCta);
   if (budget > max_smem) budget = max_smem;
-  const int64_t avail = budget - static_cast<int64_t>(Cfg::kTailBytes + Cfg::kAlignSlack);
+  const int64_t avail = budget - static_cast<int64_t>(Cfg::kTailBytes + Cfg::kAlignSlack) - extra_tail;
   if (avail <= 0) return false;
   const int64_t jmax = (U + grid - 1) / grid;
   const int64_t nkb = jmax < KB ? jmax : KB;
@@ -1085,7 +1155,7 @@ inline bool tm_plan(TmPlan* pl, int M, int64_t U, int64_t KB, int grid, int sm_c
   pl->b_off = static_cast<uint32_t>(S * kTmATileBytes);
   pl->x_off = pl->b_off + static_cast<uint32_t>(S * Cfg::kBTileBytes);
   pl->bar_off = pl->x_off + static_cast<uint32_t>(xbytes);
-  pl->smem = pl->bar_off + Cfg::kTailBytes + Cfg::kAlignSlack;
+  pl->smem = pl->bar_off + Cfg::kTailBytes + Cfg::kAlignSlack + static_cast<size_t>(extra_tail);
   return pl->smem <= static_cast<size_t>(max_smem);
 }
 
@@ -1093,8 +1163,12 @@ template <int MT, bool SW>
 int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int grid, int sm_count,
                    int max_smem, cudaStream_t stream, int resident_mode, int csize) {
   TmPlan pl;
-  if (!tm_plan<MT, SW>(&pl, p.M, p.U, p.KB, grid, sm_count, max_smem, resident_mode))
+  // add + RMSNorm: group sums and rstd per token after the ws cache, and the
+  // resident feed (the prologue is the only place the norm is computed)
+  const int64_t norm_bytes = p.norm.norm ? ((static_cast<int64_t>(p.M) * (p.KB + 1) * 4 + 15) / 16) * 16 : 0;
+  if (!tm_plan<MT, SW>(&pl, p.M, p.U, p.KB, grid, sm_count, max_smem, resident_mode, norm_bytes))
     return 8;  // FP8GQ_ERR_UNSUPPORTED
+  if (p.norm.norm && !pl.resident) return 8;
   auto fn = gemm_tm_kernel<MT, SW>;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess)
     return 7;  // FP8GQ_ERR_LAUNCH
@@ -1119,7 +1193,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
                      int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
                      float* sx_out, void* workspace, size_t workspace_bytes, int sm_count, int max_smem,
                      cudaStream_t stream, int early_weights = 0, int grid_override = 0,
-                     int resident_mode = 1, int cluster_mode = 1, const GatherParams* gather = nullptr) {
+                     int resident_mode = 1, int cluster_mode = 1, const GatherParams* gather = nullptr,
+                     const NormParams* norm = nullptr) {
   const int MT = tm_token_tile(M);
   if (N / kGroup > kTmMaxRowBlocks) return 8;  // FP8GQ_ERR_UNSUPPORTED
   const size_t need = tm_workspace_bytes_for(M, N, K, sm_count);
@@ -1137,8 +1212,21 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   p.U = static_cast<int64_t>(N / kGroup) * p.KB;
   p.counters = static_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTmCounterBytes);
-  const int grid = grid_override > 0 ? (grid_override < p.U ? grid_override : static_cast<int>(p.U))
-                                      : tm_grid(p.U, sm_count, MT, N / kGroup, p.KB);
+  int grid = grid_override > 0 ? (grid_override < p.U ? grid_override : static_cast<int>(p.U))
+                                : tm_grid(p.U, sm_count, MT, N / kGroup, p.KB);
+  if (norm && norm->norm && grid_override <= 0) {
+    // the norm needs the resident feed: if the activation of a CTA's K range
+    // does not fit next to a two-CTA-per-SM ring, use one CTA per SM
+    const int64_t jmax = (p.U + grid - 1) / grid;
+    const int64_t nkb = jmax < p.KB ? jmax : p.KB;
+    const int mp = M < MT ? M : MT;
+    if (grid > sm_count && nkb * mp * 128 > 32 * 1024) {
+      int g1 = 0;
+      for (int S = 1; S <= p.KB && S <= kTmMaxCluster; S *= 2)
+        if (p.KB % S == 0 && static_cast<int64_t>(N / kGroup) * S <= sm_count) g1 = (N / kGroup) * S;
+      grid = g1 >= sm_count / 2 ? g1 : static_cast<int>(p.U < sm_count ? p.U : sm_count);
+    }
+  }
   if (grid > tm_slots(sm_count, MT)) return 8;  // partial-sum slots exist for at most this many CTAs
   if ((p.U + grid - 1) / grid + 1 > kTmWsCache) return 8;  // FP8GQ_ERR_UNSUPPORTED: tiles per CTA
   // aligned split: every CTA takes 1/split of one row block's K range
@@ -1167,6 +1255,11 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     p.ldx = ldx;
     p.early_weights = early_weights;
     p.gather = gather ? *gather : GatherParams{};
+    p.norm = norm ? *norm : NormParams{};
+    if (norm && norm->norm) {
+      p.norm.res = norm->res + static_cast<int64_t>(m0) * norm->ldr;
+      if (norm->res_out) p.norm.res_out = norm->res_out + static_cast<int64_t>(m0) * norm->ldro;
+    }
     if (gather) {
       // this pass's rows of every rank's output; only the first pass waits
       for (int r = 0; r < gather->world; ++r) p.gather.out[r] = gather->out[r] + static_cast<int64_t>(m0) * gather->ldo;

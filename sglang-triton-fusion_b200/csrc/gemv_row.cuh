@@ -41,6 +41,7 @@ struct RowParams {
   float* sx_out;            // optional [K/128]
   int early_weights;        // weights are static: fetch the first stages before the grid-dependency wait
   GatherParams gather;      // N-sharded output written to every rank (world > 0)
+  NormParams norm;          // add + RMSNorm prologue (plain kernel only)
 };
 
 constexpr int kRowMaxConsumerThreads = 384;  // the launcher never picks T > 384
@@ -199,6 +200,44 @@ gemv_row_kernel(const RowParams p) {
   // Quantise this thread's chunks of the activation (whole 128-groups are
   // shared by 8 consecutive lanes, so the group amax is a 3-step shuffle).
   const int n_chunks = p.K / 16;
+  // add + RMSNorm: first the row's sum of squares (chunk sums, octet sums per
+  // 128-group into shared memory, then one thread adds the groups in order)
+  float rstd = 0.0f;
+  if (!kSwiglu && p.norm.norm) {
+    float* gsum = window;                 // [K/128 + 1] until the main loop
+#pragma unroll
+    for (int i = 0; i < C; ++i) {
+      const int c = tid + T * i;
+      const bool valid = c < n_chunks;
+      float sv[16];
+      if (valid) {
+        const uint4* xp = reinterpret_cast<const uint4*>(p.x + 16 * c);
+        const uint4* rp = reinterpret_cast<const uint4*>(p.norm.res + 16 * c);
+        add16(sv, xp[0], xp[1], rp[0], rp[1]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) sv[e] = 0.0f;
+      }
+      const float gs = octet_sum(sumsq16(sv));
+      if (valid && (c & 7) == 0) gsum[c >> 3] = gs;
+      if (valid && blockIdx.x == 0 && p.norm.res_out) {
+        uint4 a, b;
+        pack_bf16x16(sv, a, b);
+        uint4* op = reinterpret_cast<uint4*>(p.norm.res_out + 16 * c);
+        op[0] = a;
+        op[1] = b;
+      }
+    }
+    named_bar_sync(1, T);
+    if (tid == 0) {
+      float a = 0.0f;
+      for (int b = 0; b < p.K / 128; ++b) a = __fadd_rn(a, gsum[b]);
+      gsum[p.K / 128] = rms_rstd(a, p.K, p.norm.eps);
+    }
+    named_bar_sync(1, T);
+    rstd = gsum[p.K / 128];
+    named_bar_sync(1, T);                 // the window is reused below
+  }
   uint32_t xh[C][8];
   float sx_c[C];
   int blk[C];
@@ -222,11 +261,19 @@ gemv_row_kernel(const RowParams p) {
       } else {
         const uint4* xp = reinterpret_cast<const uint4*>(p.x + 16 * c);
         const uint4 a = xp[0], b = xp[1];
-        const uint32_t xw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        if (p.norm.norm) {
+          const uint4* rp = reinterpret_cast<const uint4*>(p.norm.res + 16 * c);
+          const uint4* wp = reinterpret_cast<const uint4*>(p.norm.w + 16 * c);
+          float sv[16];
+          add16(sv, a, b, rp[0], rp[1]);
+          norm16(v, sv, rstd, wp[0], wp[1]);
+        } else {
+          const uint32_t xw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          v[2 * e] = bf16_lo(xw[e]);
-          v[2 * e + 1] = bf16_hi(xw[e]);
+          for (int e = 0; e < 8; ++e) {
+            v[2 * e] = bf16_lo(xw[e]);
+            v[2 * e + 1] = bf16_hi(xw[e]);
+          }
         }
       }
     } else {

@@ -59,6 +59,9 @@ SIGNATURES = {
     "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "fp8gq_add_rmsnorm": (_I, [_P, _I64, _P, _I64, _P, ctypes.c_float, _P, _I64, _P, _I64, _I, _I, _P]),
+    "fp8gq_fused_add_rmsnorm_gemv_quant": (_I, [_P, _I64, _P, _I64, _P, ctypes.c_float, _P, _I64, _P, _I64,
+                                                _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "fp8gq_fused_gemv_quant_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
                                            _P, _SZ, _P]),
     "fp8gq_gather_wait": (_I, [ctypes.POINTER(Gather), _P]),

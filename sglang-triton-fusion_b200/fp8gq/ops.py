@@ -208,3 +208,63 @@ def fused_swiglu_quant(gate: torch.Tensor, up: torch.Tensor):
     _lib.check(lib.fp8gq_swiglu_quant(_ptr(gate), gate.stride(0), _ptr(up), up.stride(0), _ptr(q), q.stride(0),
                                       _ptr(scale), M, I, _stream(gate.device)), "fp8gq_swiglu_quant")
     return q, scale
+
+
+RMS_EPS = 1e-6
+
+
+def _check_norm_inputs(x, residual, weight):
+    _check_cuda(x, residual, weight)
+    for t, n in ((x, "x"), (residual, "residual")):
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+            raise TypeError(f"{n} must be a 2-D bf16 tensor, contiguous along its last dimension")
+    if weight.dtype != torch.bfloat16 or weight.dim() != 1 or not weight.is_contiguous():
+        raise TypeError("the norm weight must be a contiguous 1-D bf16 tensor")
+    if residual.shape != x.shape or weight.shape[0] != x.shape[1]:
+        raise ShapeError(f"x {tuple(x.shape)}, residual {tuple(residual.shape)} and weight "
+                         f"{tuple(weight.shape)} do not match")
+    M, K = x.shape
+    if K % GROUP:
+        raise ShapeError("K must be a multiple of 128")
+    return M, K
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = RMS_EPS, *,
+                out=None, residual_out=None):
+    """Fused add + RMSNorm (kernels/fused_rmsnorm.py:14-27): returns
+    (bf16(rmsnorm(x + residual) * weight), bf16(x + residual)); bf16 inputs,
+    fp32 math in a fixed order (include/fp8gq.h, fp8gq_add_rmsnorm)."""
+    M, K = _check_norm_inputs(x, residual, weight)
+    if out is None:
+        out = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    if residual_out is None:
+        residual_out = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    _lib.check(lib.fp8gq_add_rmsnorm(_ptr(x), x.stride(0), _ptr(residual), residual.stride(0), _ptr(weight),
+                                     float(eps), _ptr(out), out.stride(0), _ptr(residual_out),
+                                     residual_out.stride(0), M, K, _stream(x.device)), "fp8gq_add_rmsnorm")
+    return out, residual_out
+
+
+def fused_add_rmsnorm_gemv_quant(x: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor,
+                                 Wq: torch.Tensor, Ws: torch.Tensor, eps: float = RMS_EPS, *, out=None,
+                                 residual_out=None, return_quant: bool = False):
+    """GEMV(quant(rmsnorm(x + residual) * norm_weight)) without storing the
+    norm output; also returns bf16(x + residual) (the decoder's new residual).
+    Returns (out, residual_out) or, with return_quant, (out, residual_out, xq, sx)."""
+    M, K = _check_norm_inputs(x, residual, norm_weight)
+    N = _check_weight(Wq, Ws, K)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    if residual_out is None:
+        residual_out = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
+    xq, sx = _quant_out(M, K, x.device, return_quant)
+    lib = _lib.load()
+    nbytes = lib.fp8gq_workspace_bytes(M, N, K)
+    ws_buf = workspace(x.device, nbytes) if nbytes else None
+    st = lib.fp8gq_fused_add_rmsnorm_gemv_quant(
+        _ptr(x), x.stride(0), _ptr(residual), residual.stride(0), _ptr(norm_weight), float(eps), _ptr(Wq),
+        Wq.stride(0), _ptr(Ws), Ws.stride(0), _ptr(out), out.stride(0), _ptr(residual_out), residual_out.stride(0),
+        M, N, K, _ptr(xq), _ptr(sx), _ptr(ws_buf), 0 if ws_buf is None else ws_buf.numel(), _stream(x.device))
+    _lib.check(st, "fp8gq_fused_add_rmsnorm_gemv_quant")
+    return (out, residual_out, xq, sx) if return_quant else (out, residual_out)

@@ -304,6 +304,73 @@ def test_lm_head_vocab_rows(fp8gq, cuda_device, M):
     assert_close(to_f32(out), exact, 3.0)
 
 
+# ---------------------------------------------------- add + RMSNorm --
+
+def _norm_inputs(M, K, seed, dev, scale=1.0):
+    x = gpu_activation(M, K, seed, dev, std=scale, outliers=False)
+    r = gpu_activation(M, K, seed + 1, dev, std=scale, outliers=False)
+    g = torch.Generator(device=dev).manual_seed(seed + 2)
+    w = (torch.randn(K, generator=g, device=dev) * 0.1 + 1.0).bfloat16()
+    return x, r, w
+
+
+@pytest.mark.parametrize("M, K", [(1, 4096), (4, 2560), (16, 12288), (3, 128)])
+def test_add_rmsnorm_bit_exact(fp8gq, cuda_device, M, K):
+    x, r, w = _norm_inputs(M, K, 500 + M, cuda_device)
+    h, res = fp8gq.add_rmsnorm(x, r, w)
+    rh, rres, _ = O.add_rmsnorm(to_f32(x), to_f32(r), to_f32(w))
+    assert np.array_equal(to_f32(h), rh)
+    assert np.array_equal(to_f32(res), rres)
+
+
+@pytest.mark.parametrize("M, K, N", [
+    (1, 4096, 6144),    # tile kernel, resident
+    (1, 4096, 4096),    # row kernel
+    (1, 2560, 4096),    # row kernel, Qwen3-4B hidden
+    (4, 4096, 24576),   # tile kernel at M = 4
+    (16, 4096, 6144),   # M = 16: the norm forces one CTA per SM so the activation stays resident
+    (8, 2560, 19456),
+])
+def test_fused_add_rmsnorm_gemv(fp8gq, cuda_device, M, K, N):
+    """The prologue computes the same norm bits as the stand-alone kernel, so
+    the quantised bytes equal those of the unfused chain and of the oracle."""
+    x, r, w = _norm_inputs(M, K, 600 + M + K, cuda_device)
+    wq, ws = gpu_weight(N, K, 601, cuda_device)
+    out, res, xq, sx = fp8gq.fused_add_rmsnorm_gemv_quant(x, r, w, wq, ws, return_quant=True)
+    h, res2 = fp8gq.add_rmsnorm(x, r, w)
+    out2, xq2, sx2 = fp8gq.fused_gemv_quant(h, wq, ws, return_quant=True)
+    assert torch.equal(xq, xq2) and torch.equal(sx, sx2)
+    assert torch.equal(res, res2)
+    _, exact, rq, rs, rres = O.fused_add_rmsnorm_gemv_quant(to_f32(x), to_f32(r), to_f32(w), to_u8(wq), to_f32(ws))
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert np.array_equal(to_f32(res), rres)
+    assert_close(to_f32(out), exact, 3.0)
+    assert_close(to_f32(out2), exact, 3.0)
+
+
+def test_add_rmsnorm_stress_battery(fp8gq, cuda_device):
+    """benchmarks/stress_tests.py:122-146 on the GPU norm and the fused path."""
+    K = 2560
+    z = torch.zeros(4, K, dtype=torch.bfloat16, device=cuda_device)
+    w = (torch.randn(K, device=cuda_device) * 0.1).bfloat16()
+    h, res = fp8gq.add_rmsnorm(z, z, w)
+    assert bool((h == 0).all()) and bool((res == 0).all())
+    x, r, _ = _norm_inputs(8, K, 700, cuda_device, scale=1e6)
+    h, res = fp8gq.add_rmsnorm(x, r, w)
+    ref = torch.nn.functional.rms_norm(x.float() + r.float(), (K,), w.float(), 1e-6)
+    assert bool(torch.isfinite(h).all())
+    assert torch.allclose(h.float(), ref, rtol=1e-2, atol=1e-2)
+    ones = torch.ones(K, dtype=torch.bfloat16, device=cuda_device)
+    x, r, _ = _norm_inputs(4, K, 710, cuda_device)
+    h, _ = fp8gq.add_rmsnorm(x, r, ones)
+    s = x.float() + r.float()
+    manual = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6)
+    assert torch.allclose(h.float(), manual, rtol=1e-2, atol=1e-2)
+    wq, ws = gpu_weight(2560, K, 711, cuda_device)
+    with pytest.raises(fp8gq.Fp8gqError):                 # residual_out may not alias residual
+        fp8gq.fused_add_rmsnorm_gemv_quant(x, r, ones, wq, ws, residual_out=r)
+
+
 # ---------------------------------------- stand-alone SwiGLU writers --
 
 @pytest.mark.parametrize("M, I", [(512, 9728), (16, 9728), (3, 256), (1, 12288)])

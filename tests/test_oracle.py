@@ -181,6 +181,39 @@ def test_writer_formula_differs_from_gemv_prologue():
     assert sw[0, 0] != sg[0, 0] and qw[0, 0] != qg[0, 0]
 
 
+# ---------------------------------------------------- add + RMSNorm prologue --
+
+def test_add_rmsnorm_close_to_torch():
+    """The fixed-order fp32 evaluation agrees with torch's rms_norm of the
+    same sum within one bf16 rounding (kernels/fused_rmsnorm.py:74-75 asks
+    rtol 1e-4 of its fp32 outputs; ours are bf16)."""
+    rng = np.random.default_rng(1)
+    x = O.bf16_round(rng.standard_normal((4, 2560)).astype(np.float32))
+    r = O.bf16_round(rng.standard_normal((4, 2560)).astype(np.float32))
+    w = O.bf16_round((rng.standard_normal(2560) * 0.1).astype(np.float32))
+    h, res, rstd = O.add_rmsnorm(x, r, w)
+    s = torch.from_numpy(x) + torch.from_numpy(r)
+    ref = torch.nn.functional.rms_norm(s, (2560,), torch.from_numpy(w), 1e-6).numpy()
+    assert np.all(np.abs(h - ref) <= 2.0 ** -8 * np.abs(ref) + 1e-6)
+    assert np.array_equal(res, O.bf16_round(s.numpy()))
+
+
+def test_add_rmsnorm_known_answers():
+    """benchmarks/stress_tests.py:122-146: zero rows give zero outputs (rstd =
+    1/sqrt(eps)); weight 1 gives the plain normalisation; 1e6-scale inputs
+    stay finite."""
+    z = np.zeros((2, 256), np.float32)
+    h, res, rstd = O.add_rmsnorm(z, z, np.ones(256, np.float32))
+    assert np.all(h == 0) and np.all(res == 0)
+    assert rstd[0] == np.float32(1.0) / np.sqrt(np.float32(1e-6))
+    rng = np.random.default_rng(2)
+    x = O.bf16_round(rng.standard_normal((3, 512)).astype(np.float32) * 1e6)
+    h, _, _ = O.add_rmsnorm(x, np.zeros_like(x), np.ones(512, np.float32))
+    assert np.all(np.isfinite(h))
+    ms = np.mean(h.astype(np.float64) ** 2, axis=1)
+    assert np.allclose(ms, 1.0, rtol=2e-2)
+
+
 def test_torch_reference_path_agrees_with_oracle():
     """The timed CPU baseline (torch quantise / dequantise / matmul) computes
     the same function as the numpy oracle, to bf16 tolerance."""
