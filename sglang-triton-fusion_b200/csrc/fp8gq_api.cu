@@ -209,7 +209,7 @@ int check_swiglu_writer(const void* gate, int64_t ldg, const void* up, int64_t l
 // output has arrived; one thread.
 __global__ void gather_wait_kernel(const GatherParams g) {
   grid_dependency_wait();
-  if (threadIdx.x == 0) gather_wait_input(g);
+  gather_wait_input(g, threadIdx.x & 31);
   grid_launch_dependents();
 }
 

@@ -313,9 +313,6 @@ struct GatherParams {
   int wait_input;
 };
 
-__device__ __forceinline__ void st_release_sys_u32(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 __device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
   unsigned int v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -341,29 +338,34 @@ __device__ __forceinline__ void gather_cta_done(const GatherParams& g, unsigned 
     *g.counter = 0u;                     // ready for the next gathered kernel on this stream
     const unsigned int s = *g.seq + 1u;
     *g.seq = s;
+    // one system-scope release fence, then plain (relaxed, system-scope) flag stores
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
 #pragma unroll 1
-    for (int r = 0; r < g.world; ++r) st_release_sys_u32(g.flags[r] + g.rank, s);
+    for (int r = 0; r < g.world; ++r)
+      asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(g.flags[r] + g.rank), "r"(s) : "memory");
   }
 }
 
-// One thread, after grid_dependency_wait: wait (bounded) until every rank's
-// slice of this rank's last gathered output has arrived.  False (and the
-// error word set) on timeout.
-__device__ __forceinline__ bool gather_wait_input(const GatherParams& g) {
+// One warp (all 32 lanes), after grid_dependency_wait: wait (bounded) until
+// every rank's slice of this rank's last gathered output has arrived -- lane r
+// watches rank r's flag.  False on every lane (and the error word set) on
+// timeout.
+__device__ __forceinline__ bool gather_wait_input(const GatherParams& g, int lane) {
   const unsigned int s = *reinterpret_cast<volatile unsigned int*>(g.seq);
-  const unsigned int* mine = g.flags[g.rank];
-  const uint64_t t0 = global_ns();
-#pragma unroll 1
-  for (int r = 0; r < g.world; ++r) {
+  bool ok = true;
+  if (lane < g.world) {
+    const unsigned int* flag = g.flags[g.rank] + lane;
+    const uint64_t t0 = global_ns();
     for (uint32_t it = 0;; ++it) {
-      if (static_cast<int>(ld_acquire_sys_u32(mine + r) - s) >= 0) break;
+      if (static_cast<int>(ld_acquire_sys_u32(flag) - s) >= 0) break;
       if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
         record_error(kSiteGather);
-        return false;
+        ok = false;
+        break;
       }
     }
   }
-  return true;
+  return __all_sync(0xffffffffu, ok) != 0;
 }
 
 // Host: launch with programmatic stream serialization (the kernel pairs it with

@@ -497,7 +497,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   grid_dependency_wait();
   if (p.gather.wait_input) {
     // the activation is a gathered output: every rank's slice must be here
-    if (tid == 0 && !gather_wait_input(p.gather)) misc[2] = 1u;
+    if (warp == 0 && !gather_wait_input(p.gather, lane) && lane == 0) misc[2] = 1u;
     __syncthreads();
     if (misc[2]) ok = false;
   }

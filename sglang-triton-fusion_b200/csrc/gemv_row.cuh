@@ -190,7 +190,10 @@ gemv_row_kernel(const RowParams p) {
   bool in_ok = true;
   if (p.gather.wait_input) {
     // the activation is a gathered output: every rank's slice must be here
-    if (tid == 0) window[0] = gather_wait_input(p.gather) ? 1.0f : 0.0f;
+    if (warp == 0) {
+      const bool w_ok = gather_wait_input(p.gather, lane);
+      if (lane == 0) window[0] = w_ok ? 1.0f : 0.0f;
+    }
     named_bar_sync(1, T);
     in_ok = window[0] != 0.0f;
     named_bar_sync(1, T);
