@@ -55,7 +55,9 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "fp8gq_device.cuh"
 
@@ -1184,6 +1186,84 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   return cudaGetLastError() == cudaSuccess ? 0 : 7;
 }
 
+// How many clusters of `csize` CTAs with `smem` bytes each can be resident at
+// once (cudaOccupancyMaxActiveClusters), cached per device and configuration.
+template <int MT, bool SW>
+int tm_max_clusters(int csize, size_t smem, int max_smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, csize, smem);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  auto fn = gemm_tm_kernel<MT, SW>;
+  int n = 0;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(csize);
+    cfg.blockDim = dim3(kTmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, fn, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  cache[key] = n;
+  return n;
+}
+
+// Grid of a launch.  First choice: the widest aligned split S <= 8 (the S
+// CTAs of a row block share its K range and reduce in a cluster) whose grid
+// fits the resident CTA slots and whose clusters are all resident in one wave
+// (measured on B200: a second wave of clusters, e.g. 16 clusters of 8
+// one-per-SM CTAs where 15 fit, costs more than a narrower split).  Wider splits hand off
+// through the workspace and stream-K spreads the tiles over all slots; both
+// only when no cluster split of at least 2 (or with half the SMs) exists.
+// With need_resident, only grids whose plan keeps the activation resident.
+template <int MT, bool SW>
+int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem, int resident_mode,
+                   bool need_resident, int64_t extra_tail) {
+  const int64_t slots = tm_slots(sm_count, MT);
+  const int mp = M < MT ? M : MT;
+  auto usable = [&](int64_t G, bool cluster, int S) {
+    TmPlan pl;
+    if (!tm_plan<MT, SW>(&pl, mp, U, KB, static_cast<int>(G), sm_count, max_smem, resident_mode, extra_tail))
+      return false;
+    if (need_resident && !pl.resident) return false;
+    // one CTA per SM (the deep ring): the clusters must all fit at once.  The
+    // occupancy query counts one CTA per SM, which is exact here; with two
+    // per SM (G > SMs) clusters pack twice as densely and G <= slots holds.
+    const bool one_per_sm = tm_ctas_per_sm<MT>() == 1 || G <= sm_count;
+    if (cluster && one_per_sm && tm_max_clusters<MT, SW>(S, pl.smem, max_smem) < NB) return false;
+    return true;
+  };
+  int64_t best = 0;
+  for (int S = 1; S <= KB && S <= kTmMaxCluster; S *= 2) {
+    const int64_t G = static_cast<int64_t>(NB) * S;
+    if (KB % S || G > slots) continue;
+    // (the same grid whichever hand-off runs, so the results do not depend on it)
+    if (usable(G, S > 1, S)) best = G;
+  }
+  if (best > 0 && (best / NB >= 2 || best >= sm_count / 2)) return static_cast<int>(best);
+  int64_t wide = 0;
+  for (int S = 2 * kTmMaxCluster; S <= KB; S *= 2) {
+    const int64_t G = static_cast<int64_t>(NB) * S;
+    if (KB % S || G > slots) continue;
+    if (usable(G, false, S)) wide = G;
+  }
+  if (wide >= sm_count / 2) return static_cast<int>(wide);
+  for (int64_t G : {U < slots ? U : slots, U < sm_count ? U : static_cast<int64_t>(sm_count)})
+    if (usable(G, false, 1)) return static_cast<int>(G);
+  return best > 0 ? static_cast<int>(best) : 0;
+}
+
 // Runs ceil(M / MT) passes of at most MT tokens; every pass reuses the
 // workspace (its counters are zero again when a pass ends).  resident_mode 0
 // forces the streaming activation path (the resident one is used wherever it
@@ -1212,20 +1292,31 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   p.U = static_cast<int64_t>(N / kGroup) * p.KB;
   p.counters = static_cast<int*>(workspace);
   p.partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kTmCounterBytes);
-  int grid = grid_override > 0 ? (grid_override < p.U ? grid_override : static_cast<int>(p.U))
-                                : tm_grid(p.U, sm_count, MT, N / kGroup, p.KB);
-  if (norm && norm->norm && grid_override <= 0) {
-    // the norm needs the resident feed: if the activation of a CTA's K range
-    // does not fit next to a two-CTA-per-SM ring, use one CTA per SM
-    const int64_t jmax = (p.U + grid - 1) / grid;
-    const int64_t nkb = jmax < p.KB ? jmax : p.KB;
+  int grid = 0;
+  if (grid_override > 0) {
+    grid = grid_override < p.U ? grid_override : static_cast<int>(p.U);
+  } else {
+    // the add + RMSNorm prologue needs the resident feed and room for its sums
+    const bool need_res = norm && norm->norm;
     const int mp = M < MT ? M : MT;
-    if (grid > sm_count && nkb * mp * 128 > 32 * 1024) {
-      int g1 = 0;
-      for (int S = 1; S <= p.KB && S <= kTmMaxCluster; S *= 2)
-        if (p.KB % S == 0 && static_cast<int64_t>(N / kGroup) * S <= sm_count) g1 = (N / kGroup) * S;
-      grid = g1 >= sm_count / 2 ? g1 : static_cast<int>(p.U < sm_count ? p.U : sm_count);
-    }
+    const int64_t nb_bytes = need_res ? ((static_cast<int64_t>(mp) * (p.KB + 1) * 4 + 15) / 16) * 16 : 0;
+    const int NBr = N / kGroup;
+    if (MT == 16)
+      grid = swiglu ? tm_choose_grid<16, true>(NBr, p.KB, p.U, M, sm_count, max_smem, resident_mode, need_res,
+                                               nb_bytes)
+                    : tm_choose_grid<16, false>(NBr, p.KB, p.U, M, sm_count, max_smem, resident_mode, need_res,
+                                                nb_bytes);
+    else if (MT == 32)
+      grid = swiglu ? tm_choose_grid<32, true>(NBr, p.KB, p.U, M, sm_count, max_smem, resident_mode, need_res,
+                                               nb_bytes)
+                    : tm_choose_grid<32, false>(NBr, p.KB, p.U, M, sm_count, max_smem, resident_mode, need_res,
+                                                nb_bytes);
+    else
+      grid = swiglu ? tm_choose_grid<64, true>(NBr, p.KB, p.U, M, sm_count, max_smem, resident_mode, need_res,
+                                               nb_bytes)
+                    : tm_choose_grid<64, false>(NBr, p.KB, p.U, M, sm_count, max_smem, resident_mode, need_res,
+                                                nb_bytes);
+    if (grid <= 0) return 8;  // FP8GQ_ERR_UNSUPPORTED: no plan fits
   }
   if (grid > tm_slots(sm_count, MT)) return 8;  // partial-sum slots exist for at most this many CTAs
   if ((p.U + grid - 1) / grid + 1 > kTmWsCache) return 8;  // FP8GQ_ERR_UNSUPPORTED: tiles per CTA

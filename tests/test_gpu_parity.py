@@ -216,7 +216,7 @@ def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
     (1, 4096, 4096, False),     # K range split 8 ways: a cluster of 8 CTAs per row block (slot = tile)
     (2, 4096, 6144, False),     # a cluster of 4
     (3, 2560, 4096, False),
-    (4, 4096, 1152, False),     # split 32 ways: beyond a cluster, the hand-off goes through the workspace
+    (4, 4096, 1152, False),     # 9 row blocks: a cluster of 8 per row block, one CTA per SM
     (2, 10368, 896, False),     # stream-K: CTA ranges cross row blocks, K blocks wrap
     (16, 1024, 1280, False),    # 16 tokens x 8 K blocks: a large resident footprint
     (16, 4096, 6144, False),    # too large to be resident next to a 2-CTA-per-SM ring
