@@ -162,15 +162,8 @@ int launch_quant(bool swiglu, const void* x, int64_t ldx, int M, int K, uint8_t*
   DeviceInfo di;
   int st = device_info(&di, nullptr);
   if (st != FP8GQ_OK) return st;
-  const int64_t groups = static_cast<int64_t>(M) * (K / kGroup);
-  const int64_t blocks = (groups + 7) / 8;
-  if (blocks > 0x7fffffff) return FP8GQ_ERR_UNSUPPORTED;
-  if (swiglu)
-    group_quant_kernel<true><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), ldx, M, K, xq, sx);
-  else
-    group_quant_kernel<false><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), ldx, M, K, xq, sx);
+  if (launch_group_quant(swiglu, static_cast<const __nv_bfloat16*>(x), ldx, M, K, xq, sx, stream) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
   return launch_status();
 }
 

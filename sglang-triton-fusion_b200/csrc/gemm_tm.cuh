@@ -60,6 +60,7 @@
 #include <tuple>
 
 #include "fp8gq_device.cuh"
+#include "quant_only.cuh"
 
 namespace fp8gq {
 
@@ -107,6 +108,8 @@ struct TmParams {
   const __nv_bfloat16* x;   // activation rows of this pass (resident mode reads them directly)
   int64_t ldx;
   int resident;             // resident activation mode
+  int prequant;             // pre-quantised feed: B tiles by TMA from xq (tmap_x), scales from sx_pre
+  const float* sx_pre;      // [M, K/128] scales of the pre-quantised activation
   int csize;                // split-K cluster size (1: none; the CTAs of a row block form a cluster)
   int early_weights;        // weights and block scales are static: load them before the grid-dependency wait
   int* counters;            // [kTmMaxRowBlocks], zero on entry and exit
@@ -365,7 +368,7 @@ __device__ __forceinline__ void tm_touch_params(const TmParams& p) {
                reinterpret_cast<uint64_t>(p.xq_out) ^ reinterpret_cast<uint64_t>(p.sx_out);
   uint32_t u = static_cast<uint32_t>(p.M ^ p.sw ^ p.lg_sw ^ p.kpb ^ p.nacc ^ p.stages ^ p.npw ^ p.N ^ p.K ^ p.KB ^
                                      p.resident ^ p.csize ^ p.early_weights ^ p.gather.world ^
-                                     p.gather.wait_input ^ p.norm.norm) ^
+                                     p.gather.wait_input ^ p.norm.norm ^ p.prequant) ^
                p.b_off ^ p.x_off ^ p.bar_off ^ p.x_tile_bytes;
   asm volatile("" ::"l"(t), "r"(u));
 }
@@ -422,6 +425,13 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // (J >= KB) keeps every K block, slot = kb; otherwise its J tiles have J
   // distinct K blocks (kb0, kb0 + 1, ... mod KB), slot = j.
   const bool resident = p.resident != 0;
+  // Pre-quantised feed (large M, where the resident feed does not fit and
+  // every CTA would otherwise quantise the same activation): a group-quant
+  // kernel ran just before this one; B tiles arrive by TMA with the weight
+  // tiles (the e4m3 rows land K-major in the 128-byte swizzle, rows past M
+  // are zero-filled), scales are loaded like the resident ones.
+  const bool prequant = p.prequant != 0;
+  const bool sx_res = resident || prequant;    // scales of the K range in shared memory from the prologue
   const bool res_full = J >= p.KB;
   const int nkb = res_full ? p.KB : J;
   // the CTA's first tile (row block nb0, K block kb0): the only 64-bit
@@ -442,7 +452,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       if (!resident) prefetch_tensormap(&tmap_x);
     }
     if (lane < S) {
-      mbar_init(&full[lane], 1 + 1);     // TMA arrive_expect_tx + the activation warp of the K block
+      mbar_init(&full[lane], prequant ? 1 : 2);   // TMA arrive_expect_tx (+ the activation warp of the K block)
       mbar_init(&xfull[lane], 1);        // TMA arrive_expect_tx (activation tile)
       mbar_init(&empty[lane], 1);        // tcgen05.commit
     }
@@ -475,7 +485,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // overlapping the previous kernel's tail.  Activations, outputs and the
   // workspace are touched only after it.
   const bool early = p.early_weights != 0;
-  const int n_pre = early ? (J < S ? J : S) : 0;
+  const int n_pre = (early && !prequant) ? (J < S ? J : S) : 0;
   auto ws_at = [&](int j) {
     const int t = kb0 + j;
     const int dn = t / p.KB;
@@ -666,6 +676,16 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
       }
     }
+    if (prequant) {
+      // scales of the CTA's K range, [slot][M] as in the resident feed
+      for (int i = tid - 64; i < nkb * p.M; i += kTmThreads - 64) {
+        const int r = i / p.M;
+        const int m = i - r * p.M;
+        int kb = res_full ? r : kb0 + r;
+        if (kb >= p.KB) kb -= p.KB;
+        sx_ring[i] = __ldcg(p.sx_pre + static_cast<int64_t>(m) * p.KB + kb);
+      }
+    }
     if (!early) {
       if (jw < J) ws_cache[jw] = ws_first;
       for (int j = jw + (kTmThreads - 64); j < J; j += kTmThreads - 64) ws_cache[j] = ws_at(j);
@@ -689,11 +709,15 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const int s = c.s;
         if (j >= S) ok = mbar_wait(&empty[s], c.ph ^ 1u, kSiteTmA);
         if (!ok) break;
-        if (j >= n_pre) {
+        if (prequant) {
+          mbar_arrive_expect_tx(&full[s], kTmATileBytes + Cfg::kBTileBytes);
+          tma_load_2d(a_tiles + s * kTmATileBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[s], pol_w);
+          tma_load_2d(b_tiles + s * Cfg::kBTileBytes, &tmap_x, c.kb * 128, 0, &full[s], pol_x);
+        } else if (j >= n_pre) {
           mbar_arrive_expect_tx(&full[s], kTmATileBytes);
           tma_load_2d(a_tiles + s * kTmATileBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[s], pol_w);
         }
-        if (!resident) {
+        if (!resident && !prequant) {
           uint8_t* xt = x_tiles + s * static_cast<uint32_t>(Cfg::kXTileBytes);
           mbar_arrive_expect_tx(&xfull[s], xbytes);
           tma_load_2d(xt, &tmap_x, c.kb * 128, 0, &xfull[s], pol_x);
@@ -706,7 +730,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         // let the copies already issued land before the CTA can exit
         for (int j = (issued > S ? issued - S : 0); j < issued; ++j) {
           mbar_wait(&full[j % S], (j / S) & 1, kSiteTmA);
-          if (!resident) mbar_wait(&xfull[j % S], (j / S) & 1, kSiteTmA);
+          if (!resident && !prequant) mbar_wait(&xfull[j % S], (j / S) & 1, kSiteTmA);
         }
       }
     }
@@ -759,7 +783,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     TileCursor c;
     c.init(nb0, kb0);
     for (int k = 0; k < j_first; ++k) c.next(p.KB, kpb, S);
-    for (int j = j_first; w4 < NPW && j < J && ok; j += NPW) {
+    for (int j = j_first; w4 < NPW && !prequant && j < J && ok; j += NPW) {
       if (j > j_first) {
         for (int k = 0; k < NPW; ++k) c.next(p.KB, kpb, S);
       }
@@ -873,7 +897,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         use = q <= pos && m < p.M;
         const int qc = use ? q : 0;
         const int mc = use ? m : 0;
-        const int si = resident ? (rq0 + qc) * p.M + mc : ((jq0 + qc) & (kTmSxRing - 1)) * MT + mc;
+        const int si = sx_res ? (rq0 + qc) * p.M + mc : ((jq0 + qc) & (kTmSxRing - 1)) * MT + mc;
         return sx_ring[si] * ws_cache[jq0 + qc];
       };
       constexpr bool kPre = MT == 16;         // the 16-token tile: all scales in registers up front
@@ -889,15 +913,15 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           }
         }
       };
-      if (resident) load_scales();
+      if (sx_res) load_scales();
       if (ok) ok = mbar_wait(&acc_full[a], accc.round, kSiteTmAcc);
-      if (!resident && lane == 0) {
+      if (!sx_res && lane == 0) {
         for (int q = 0; q <= pos && ok; ++q) ok = tag_wait(sx_tag + ((j - pos + q) & (kTmSxRing - 1)),
                                                          static_cast<uint32_t>(j - pos + q + 1));
         __threadfence_block();
       }
       ok = __all_sync(0xffffffffu, ok) != 0;   // tcgen05.ld below is warp-collective
-      if (!resident) load_scales();
+      if (!sx_res) load_scales();
       tc_fence_after();
 #pragma unroll
       for (int c16 = 0; c16 < MT / 16; ++c16) {
@@ -1056,11 +1080,28 @@ inline int tm_grid(int64_t U, int sm_count, int MT, int NB = 0, int KB = 0) {
   return static_cast<int>(U < slots ? U : slots);
 }
 
-inline size_t tm_workspace_bytes_for(int M, int N, int K, int sm_count) {
+// Whether M tokens may take the pre-quantised feed: every pass has one K
+// block per accumulator group (16-token tile with M > 8, or a wider tile).
+inline bool tm_prequant_shape(int M) { return M > 8; }
+
+inline size_t tm_align256(size_t b) { return (b + 255) / 256 * 256; }
+
+// Workspace: split-K counters, partial sums of up to one CTA per resident
+// slot, and (shapes that may be pre-quantised) the quantised activation and
+// its scales.
+inline size_t tm_partials_end(int M, int N, int K, int sm_count) {
   const int MT = tm_token_tile(M);
   const int64_t U = static_cast<int64_t>(N / kGroup) * (K / kGroup);
   const int G = tm_slots(sm_count, MT) < U ? tm_slots(sm_count, MT) : static_cast<int>(U);
   return kTmCounterBytes + static_cast<size_t>(G) * 2 * MT * 128 * sizeof(float);
+}
+
+inline size_t tm_workspace_bytes_for(int M, int N, int K, int sm_count) {
+  size_t b = tm_partials_end(M, N, K, sm_count);
+  if (tm_prequant_shape(M))
+    b = tm_align256(b) + tm_align256(static_cast<size_t>(M) * K) +
+        tm_align256(static_cast<size_t>(M) * (K / kGroup) * sizeof(float));
+  return b;
 }
 
 inline size_t tm_workspace_bytes(int M, int N, int K) {
@@ -1097,6 +1138,21 @@ inline bool make_weight_tmap(CUtensorMap* map, const void* w, int N, int K, int6
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Pre-quantised activation map: 2-D uint8 [rows, K] (row stride K), box 128
+// bytes x MT rows in the 128-byte swizzle -- a B tile; rows past `rows` are
+// zero-filled.
+inline bool make_xq_tmap(CUtensorMap* map, const void* xq, int rows, int K, int MT) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+  cuuint32_t box[2] = {128, static_cast<cuuint32_t>(MT)};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(xq), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Activation tensor map: 2-D bf16 [rows, cols] with row stride ldx elements,
 // box 128 columns x `rows` rows, no swizzle (rows land 256 bytes apart).
 inline bool make_act_tmap(CUtensorMap* map, const void* x, int rows, int64_t cols, int64_t ldx) {
@@ -1124,7 +1180,7 @@ struct TmPlan {
 // scales in the sx ring -- is used when it still leaves at least 4 stages.
 template <int MT, bool SW>
 inline bool tm_plan(TmPlan* pl, int M, int64_t U, int64_t KB, int grid, int sm_count, int max_smem,
-                    int resident_mode, int64_t extra_tail = 0) {
+                    int resident_mode, int64_t extra_tail = 0, bool prequant = false) {
   using Cfg = TmCfg<MT, SW>;
   const bool one_per_sm = tm_ctas_per_sm<MT>() == 1 || grid <= sm_count;
   int64_t budget = one_per_sm ? max_smem
@@ -1146,7 +1202,11 @@ inline bool tm_plan(TmPlan* pl, int M, int64_t U, int64_t KB, int grid, int sm_c
       xbytes = rbytes;
     }
   }
-  if (!res) {
+  if (!res && prequant) {
+    // B tiles come by TMA like the weight tiles: no activation region
+    S = tm_pick_stages(avail / (kTmATileBytes + Cfg::kBTileBytes));
+    xbytes = 0;
+  } else if (!res) {
     S = tm_pick_stages(avail / (kTmATileBytes + Cfg::kBTileBytes + Cfg::kXTileBytes));
     xbytes = static_cast<int64_t>(S) * Cfg::kXTileBytes;
   }
@@ -1168,7 +1228,8 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   // add + RMSNorm: group sums and rstd per token after the ws cache, and the
   // resident feed (the prologue is the only place the norm is computed)
   const int64_t norm_bytes = p.norm.norm ? ((static_cast<int64_t>(p.M) * (p.KB + 1) * 4 + 15) / 16) * 16 : 0;
-  if (!tm_plan<MT, SW>(&pl, p.M, p.U, p.KB, grid, sm_count, max_smem, resident_mode, norm_bytes))
+  if (!tm_plan<MT, SW>(&pl, p.M, p.U, p.KB, grid, sm_count, max_smem, p.prequant ? 0 : resident_mode, norm_bytes,
+                       p.prequant != 0))
     return 8;  // FP8GQ_ERR_UNSUPPORTED
   if (p.norm.norm && !pl.resident) return 8;
   auto fn = gemm_tm_kernel<MT, SW>;
@@ -1326,6 +1387,37 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   const bool aligned = split > 0 && p.KB % split == 0;
   const int csize = (cluster_mode != 0 && aligned && split >= 2 && split <= kTmMaxCluster) ? split : 1;
   const int64_t xcols = swiglu ? 2 * static_cast<int64_t>(K) : K;
+  // Pre-quantised feed: large M whose activation does not stay resident at
+  // this grid -- quantise it once here (into xq_out / sx_out when given, else
+  // the workspace) instead of in every CTA.
+  bool pre = false;
+  uint8_t* pre_xq = nullptr;
+  float* pre_sx = nullptr;
+  if (resident_mode != 0 && tm_prequant_shape(M) && !(norm && norm->norm)) {
+    const int mp0 = M < MT ? M : MT;
+    TmPlan pl0;
+    bool ok0;
+    if (MT == 16)
+      ok0 = swiglu ? tm_plan<16, true>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode)
+                   : tm_plan<16, false>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode);
+    else if (MT == 32)
+      ok0 = swiglu ? tm_plan<32, true>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode)
+                   : tm_plan<32, false>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode);
+    else
+      ok0 = swiglu ? tm_plan<64, true>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode)
+                   : tm_plan<64, false>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode);
+    const int64_t jmax = (p.U + grid - 1) / grid;
+    const int64_t nkb = jmax < p.KB ? jmax : p.KB;
+    pre = !(ok0 && pl0.resident) && nkb * mp0 <= static_cast<int64_t>(kTmSxRing) * MT;
+  }
+  if (pre) {
+    uint8_t* region = static_cast<uint8_t*>(workspace) + tm_align256(tm_partials_end(M, N, K, sm_count));
+    pre_xq = xq_out ? xq_out : region;
+    pre_sx = sx_out ? sx_out : reinterpret_cast<float*>(region + tm_align256(static_cast<size_t>(M) * K));
+    if (launch_group_quant(swiglu, static_cast<const __nv_bfloat16*>(x), ldx, M, K, pre_xq, pre_sx, stream) !=
+        cudaSuccess)
+      return 7;
+  }
   for (int m0 = 0; m0 < M; m0 += MT) {
     const __nv_bfloat16* xp = static_cast<const __nv_bfloat16*>(x) + static_cast<int64_t>(m0) * ldx;
     p.out = static_cast<__nv_bfloat16*>(out) + static_cast<int64_t>(m0) * ldo;
@@ -1356,10 +1448,16 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
       for (int r = 0; r < gather->world; ++r) p.gather.out[r] = gather->out[r] + static_cast<int64_t>(m0) * gather->ldo;
       if (m0 > 0) p.gather.wait_input = 0;
     }
-    p.xq_out = xq_out ? xq_out + static_cast<int64_t>(m0) * K : nullptr;
-    p.sx_out = sx_out ? sx_out + static_cast<int64_t>(m0) * (K / kGroup) : nullptr;
+    p.xq_out = (xq_out && !pre) ? xq_out + static_cast<int64_t>(m0) * K : nullptr;
+    p.sx_out = (sx_out && !pre) ? sx_out + static_cast<int64_t>(m0) * (K / kGroup) : nullptr;
+    p.prequant = pre ? 1 : 0;
+    p.sx_pre = pre ? pre_sx + static_cast<int64_t>(m0) * p.KB : nullptr;
     CUtensorMap tmap_x;
-    if (!make_act_tmap(&tmap_x, xp, p.M, xcols, ldx)) return 7;
+    if (pre) {
+      if (!make_xq_tmap(&tmap_x, pre_xq + static_cast<int64_t>(m0) * K, p.M, K, MT)) return 7;
+    } else if (!make_act_tmap(&tmap_x, xp, p.M, xcols, ldx)) {
+      return 7;
+    }
     int st;
     if (MT == 16)
       st = swiglu ? launch_tm_pass<16, true>(tmap_w, tmap_x, p, grid, sm_count, max_smem, stream, resident_mode, csize)

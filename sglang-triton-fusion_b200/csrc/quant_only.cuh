@@ -1,6 +1,7 @@
 // Stand-alone activation group quant (and SwiGLU + group quant): one warp
 // per 128-group, 4 values per lane.  Same device functions as the fused
-// kernels' prologues, so its bytes are the fused kernels' bytes.
+// kernels' prologues, so its bytes are the fused kernels' bytes.  The tile
+// kernel also runs it ahead of itself for large M (its pre-quantised feed).
 #pragma once
 
 #include "fp8gq_device.cuh"
@@ -12,6 +13,8 @@ __global__ void __launch_bounds__(256) group_quant_kernel(const __nv_bfloat16* _
                                                           int64_t ldx, int M, int K,
                                                           uint8_t* __restrict__ xq,
                                                           float* __restrict__ sx_out) {
+  grid_dependency_wait();   // the activation comes from the stream's previous work
+  grid_launch_dependents();
   const int groups_per_row = K / kGroup;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * (blockDim.x / 32) + threadIdx.x / 32;
   if (gid >= static_cast<int64_t>(M) * groups_per_row) return;
@@ -42,6 +45,18 @@ __global__ void __launch_bounds__(256) group_quant_kernel(const __nv_bfloat16* _
   const uint32_t q = quant_pair(v[0], v[1], sinv) | (static_cast<uint32_t>(quant_pair(v[2], v[3], sinv)) << 16);
   *reinterpret_cast<uint32_t*>(xq + static_cast<int64_t>(m) * K + col) = q;
   if (lane == 0) sx_out[static_cast<int64_t>(m) * groups_per_row + b] = s;
+}
+
+// Launch over M rows of K (programmatic dependent launch).
+inline cudaError_t launch_group_quant(bool swiglu, const __nv_bfloat16* x, int64_t ldx, int M, int K, uint8_t* xq,
+                                     float* sx, cudaStream_t stream) {
+  const int64_t groups = static_cast<int64_t>(M) * (K / kGroup);
+  const int64_t blocks = (groups + 7) / 8;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
+  return swiglu ? launch_with_pdl(group_quant_kernel<true>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0, stream,
+                                  x, ldx, M, K, xq, sx)
+                : launch_with_pdl(group_quant_kernel<false>, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                                  stream, x, ldx, M, K, xq, sx);
 }
 
 }  // namespace fp8gq

@@ -219,7 +219,9 @@ def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
     (4, 4096, 1152, False),     # 9 row blocks: a cluster of 8 per row block, one CTA per SM
     (2, 10368, 896, False),     # stream-K: CTA ranges cross row blocks, K blocks wrap
     (16, 1024, 1280, False),    # 16 tokens x 8 K blocks: a large resident footprint
-    (16, 4096, 6144, False),    # too large to be resident next to a 2-CTA-per-SM ring
+    (16, 4096, 6144, False),    # 16 tokens x 8 K blocks per CTA: resident
+    (16, 4096, 24576, False),   # 16 tokens x 32 K blocks: pre-quantised feed (B tiles by TMA)
+    (12, 12288, 4096, True),    # pre-quantised SwiGLU feed
     (40, 2048, 2560, False),    # 64-token tile
     (1, 12288, 4096, True),
     (2, 12288, 4096, True),
