@@ -900,16 +900,37 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         const int si = sx_res ? (rq0 + qc) * p.M + mc : ((jq0 + qc) & (kTmSxRing - 1)) * MT + mc;
         return sx_ring[si] * ws_cache[jq0 + qc];
       };
+      // One K block per group (kpb == 1, i.e. sw == MT): column c is token c of
+      // K block jq0, and its sx values are contiguous -- the resident slot
+      // rq0's M entries, or streaming ring row jq0 -- so they are read at fixed
+      // offsets from one base, without col_scale's per-column index arithmetic
+      // (which costs more than the rest of the per-K-block epilogue).  Columns
+      // c >= M read on past the slot, still inside the sx ring and ws cache
+      // regions (nkb * M <= kTmSxRing * MT), and are masked off.  Same products
+      // as col_scale, so the results do not change.
+      const bool one_kb = kpb == 1;
+      const float* sx_grp = sx_res ? sx_ring + rq0 * p.M : sx_ring + (jq0 & (kTmSxRing - 1)) * MT;
+      auto live_mask = [&](int c0) -> uint32_t {   // columns c0 .. c0 + 15 that hold a token
+        const int n = p.M - c0;
+        return n >= 16 ? 0xffffu : n <= 0 ? 0u : (1u << n) - 1u;
+      };
       constexpr bool kPre = MT == 16;         // the 16-token tile: all scales in registers up front
       float scl[16];
       uint32_t pre_mask = 0;                   // bit c: column c holds a live (token, K block)
       auto load_scales = [&]() {
         if constexpr (kPre) {
+          if (one_kb) {
+            const float wsv = ws_cache[jq0];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            bool u;
-            scl[c] = col_scale(c, u);
-            pre_mask |= u ? (1u << c) : 0u;
+            for (int c = 0; c < 16; ++c) scl[c] = sx_grp[c] * wsv;
+            pre_mask = live_mask(0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              bool u;
+              scl[c] = col_scale(c, u);
+              pre_mask |= u ? (1u << c) : 0u;
+            }
           }
         }
       };
@@ -932,6 +953,11 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
           for (int i = 0; i < 16; ++i) sc[i] = scl[i];
           m16 = pre_mask;
+        } else if (one_kb) {
+          const float wsv = ws_cache[jq0];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) sc[i] = sx_grp[16 * c16 + i] * wsv;
+          m16 = live_mask(16 * c16);
         } else {
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
