@@ -239,15 +239,25 @@ int fp8gq_set_static_weights(int enable);
  *       quantising the activation of its whole K range into shared memory once,
  *       before its weight stream starts); every K block's activation tile then
  *       travels with its weight tile and is quantised on arrival;
+ *   FP8GQ_TM_PREQUANT_ACTIVATIONS  use the pre-quantised feed wherever its
+ *       scales fit: one group-quant launch writes the e4m3 activation and its
+ *       scales before the tile kernel, whose B tiles then arrive by TMA next to
+ *       the weight tiles (by default it is used where the activation cannot
+ *       stay resident, or where quantising it in every CTA costs more);
+ *   FP8GQ_TM_RESIDENT_ACTIVATIONS  use the resident feed wherever it fits and
+ *       the pre-quantised one only where it does not;
  *   FP8GQ_TM_WORKSPACE_SPLITK   never reduce split-K partial sums inside a
  *       thread-block cluster (over distributed shared memory); they go through
  *       the workspace and the last CTA of the row block adds them.
- * Every combination gives bit-identical results (same products, same order of
- * additions); the switches exist for testing and measurement.  Process-wide;
- * returns the previous mask, or -1 for unknown bits.  No counterpart in the
- * reference. */
+ * At most one of the three activation-feed bits may be set.  Every combination
+ * gives bit-identical results (same products, same order of additions); the
+ * switches exist for testing and measurement.  Process-wide; returns the
+ * previous mask, or -1 for unknown bits or two feed bits.  No counterpart in
+ * the reference. */
 #define FP8GQ_TM_STREAM_ACTIVATIONS 1
 #define FP8GQ_TM_WORKSPACE_SPLITK 2
+#define FP8GQ_TM_PREQUANT_ACTIVATIONS 4
+#define FP8GQ_TM_RESIDENT_ACTIVATIONS 8
 int fp8gq_set_tm_options(int flags);
 
 /* Reads (and with clear != 0 resets) the current device's error word, which
@@ -267,9 +277,9 @@ int fp8gq_device_error(uint32_t *code, int clear);
  * The tile kernel's split-K scratch lives instead in one fixed device array
  * of FP8GQ_NOALLOC_SCRATCH_BYTES (8 MiB) inside libfp8gq, which every GPU
  * that loads the library keeps until the process exits.  That bounds the
- * shapes: a call whose scratch (fp8gq_workspace_bytes for M >= 2) exceeds
- * the array returns FP8GQ_ERR_SCRATCH_LIMIT; on a 148-SM B200 every M <= 16
- * with N <= 524288 fits.
+ * shapes: a call whose scratch (fp8gq_workspace_bytes of the tile kernel)
+ * exceeds the array returns FP8GQ_ERR_SCRATCH_LIMIT; on a 148-SM B200 every
+ * M <= 16 with N <= 524288 and K <= 131072 fits.
  *
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before any stream

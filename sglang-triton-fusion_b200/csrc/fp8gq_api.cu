@@ -32,7 +32,12 @@ DeviceInfo g_dev[kMaxDevices];
 std::atomic<int> g_static_weights{0};
 std::atomic<int> g_tm_options{0};   // FP8GQ_TM_* bits
 
-int tm_resident_mode() { return (g_tm_options.load(std::memory_order_relaxed) & FP8GQ_TM_STREAM_ACTIVATIONS) ? 0 : 1; }
+// launch_tm's activation-feed mode for the option bits (at most one feed bit is set)
+int tm_resident_mode() {
+  const int f = g_tm_options.load(std::memory_order_relaxed);
+  return (f & FP8GQ_TM_STREAM_ACTIVATIONS) ? 0 : (f & FP8GQ_TM_PREQUANT_ACTIVATIONS) ? 2
+         : (f & FP8GQ_TM_RESIDENT_ACTIVATIONS) ? 3 : 1;
+}
 int tm_cluster_mode() { return (g_tm_options.load(std::memory_order_relaxed) & FP8GQ_TM_WORKSPACE_SPLITK) ? 0 : 1; }
 
 int device_info(DeviceInfo* out, int* dev_out) {
@@ -504,7 +509,10 @@ int fp8gq_set_static_weights(int enable) {
 }
 
 int fp8gq_set_tm_options(int flags) {
-  if (flags & ~(FP8GQ_TM_STREAM_ACTIVATIONS | FP8GQ_TM_WORKSPACE_SPLITK)) return -1;
+  constexpr int kFeed = FP8GQ_TM_STREAM_ACTIVATIONS | FP8GQ_TM_PREQUANT_ACTIVATIONS | FP8GQ_TM_RESIDENT_ACTIVATIONS;
+  if (flags & ~(kFeed | FP8GQ_TM_WORKSPACE_SPLITK)) return -1;
+  const int feed = flags & kFeed;
+  if (feed & (feed - 1)) return -1;   // more than one activation feed
   return g_tm_options.exchange(flags);
 }
 

@@ -710,9 +710,12 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         if (j >= S) ok = mbar_wait(&empty[s], c.ph ^ 1u, kSiteTmA);
         if (!ok) break;
         if (prequant) {
+          // the box's MT rows start at row -pos * sw of the M-row tensor: the
+          // tokens land in rows pos * sw + m of the B tile, every other row is
+          // the zero fill of a row outside the tensor
           mbar_arrive_expect_tx(&full[s], kTmATileBytes + Cfg::kBTileBytes);
           tma_load_2d(a_tiles + s * kTmATileBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[s], pol_w);
-          tma_load_2d(b_tiles + s * Cfg::kBTileBytes, &tmap_x, c.kb * 128, 0, &full[s], pol_x);
+          tma_load_2d(b_tiles + s * Cfg::kBTileBytes, &tmap_x, c.kb * 128, -(c.pos * p.sw), &full[s], pol_x);
         } else if (j >= n_pre) {
           mbar_arrive_expect_tx(&full[s], kTmATileBytes);
           tma_load_2d(a_tiles + s * kTmATileBytes, &tmap_w, c.kb * 128, c.nb * 128, &full[s], pol_w);
@@ -924,6 +927,14 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
             for (int c = 0; c < 16; ++c) scl[c] = sx_grp[c] * wsv;
             pre_mask = live_mask(0);
+          } else if (sx_res && p.M == p.sw) {
+            // M a power of two: the group's pos + 1 K blocks fill columns
+            // 0 .. (pos + 1) * M - 1 and their sx values are contiguous too
+            // (slots rq0, rq0 + 1, ... of M entries each); the ws index is
+            // clamped to the group's last K block
+#pragma unroll
+            for (int c = 0; c < 16; ++c) scl[c] = sx_grp[c] * ws_cache[jq0 + min(c >> p.lg_sw, pos)];
+            pre_mask = live_mask(p.M - (pos + 1) * p.sw);
           } else {
 #pragma unroll
             for (int c = 0; c < 16; ++c) {
@@ -1108,7 +1119,13 @@ inline int tm_grid(int64_t U, int sm_count, int MT, int NB = 0, int KB = 0) {
 
 // Whether M tokens may take the pre-quantised feed: every pass has one K
 // block per accumulator group (16-token tile with M > 8, or a wider tile).
-inline bool tm_prequant_shape(int M) { return M > 8; }
+// The pre-quantised feed may serve any M (the workspace then holds the
+// quantised activation); the auto choice takes it where the activation cannot
+// stay resident, or where the resident prologue -- every CTA quantising M x
+// (its K blocks) groups of the same activation -- would cost more than the
+// group-quant launch: M x (K blocks per CTA) >= kTmPrequantMinGroups.
+inline bool tm_prequant_shape(int M) { return M >= 1; }
+constexpr int64_t kTmPrequantMinGroups = 72;
 
 inline size_t tm_align256(size_t b) { return (b + 255) / 256 * 256; }
 
@@ -1165,7 +1182,8 @@ inline bool make_weight_tmap(CUtensorMap* map, const void* w, int N, int K, int6
 }
 
 // Pre-quantised activation map: 2-D uint8 [rows, K] (row stride K), box 128
-// bytes x MT rows in the 128-byte swizzle -- a B tile; rows past `rows` are
+// bytes x MT rows in the 128-byte swizzle -- a B tile; rows outside the tensor
+// (past `rows`, or before row 0 when the load starts at a negative row) are
 // zero-filled.
 inline bool make_xq_tmap(CUtensorMap* map, const void* xq, int rows, int K, int MT) {
   auto enc = tensor_map_encoder();
@@ -1352,10 +1370,13 @@ int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem,
 }
 
 // Runs ceil(M / MT) passes of at most MT tokens; every pass reuses the
-// workspace (its counters are zero again when a pass ends).  resident_mode 0
-// forces the streaming activation path (the resident one is used wherever it
-// fits otherwise); cluster_mode 0 forces the split-K hand-off through the
-// workspace (clusters are used for aligned splits of 2 to 8 CTAs otherwise).
+// workspace (its counters are zero again when a pass ends).  resident_mode
+// picks the activation feed: 0 streaming only; 1 auto (resident where it fits,
+// pre-quantised where it does not or where the resident prologue costs more:
+// kTmPrequantMinGroups); 2 pre-quantised wherever its scales fit; 3 resident
+// wherever it fits, pre-quantised only where it does not.  cluster_mode 0
+// forces the split-K hand-off through the workspace (clusters are used for
+// aligned splits of 2 to 8 CTAs otherwise).
 inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
                      int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
                      float* sx_out, void* workspace, size_t workspace_bytes, int sm_count, int max_smem,
@@ -1434,7 +1455,10 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
                    : tm_plan<64, false>(&pl0, mp0, p.U, p.KB, grid, sm_count, max_smem, resident_mode);
     const int64_t jmax = (p.U + grid - 1) / grid;
     const int64_t nkb = jmax < p.KB ? jmax : p.KB;
-    pre = !(ok0 && pl0.resident) && nkb * mp0 <= static_cast<int64_t>(kTmSxRing) * MT;
+    const bool legal = nkb * mp0 <= static_cast<int64_t>(kTmSxRing) * MT;   // scales fit the sx region
+    const bool res_fits = ok0 && pl0.resident;
+    pre = legal && (resident_mode == 2 || !res_fits ||
+                    (resident_mode == 1 && nkb * mp0 >= kTmPrequantMinGroups));
   }
   if (pre) {
     uint8_t* region = static_cast<uint8_t*>(workspace) + tm_align256(tm_partials_end(M, N, K, sm_count));

@@ -131,17 +131,20 @@ def set_static_weights(enable: bool) -> bool:
     return bool(load().fp8gq_set_static_weights(1 if enable else 0))
 
 
-TM_STREAM_ACTIVATIONS = 1   # FP8GQ_TM_STREAM_ACTIVATIONS
-TM_WORKSPACE_SPLITK = 2     # FP8GQ_TM_WORKSPACE_SPLITK
+TM_STREAM_ACTIVATIONS = 1     # FP8GQ_TM_STREAM_ACTIVATIONS
+TM_WORKSPACE_SPLITK = 2       # FP8GQ_TM_WORKSPACE_SPLITK
+TM_PREQUANT_ACTIVATIONS = 4   # FP8GQ_TM_PREQUANT_ACTIVATIONS
+TM_RESIDENT_ACTIVATIONS = 8   # FP8GQ_TM_RESIDENT_ACTIVATIONS
 
 
 def set_tm_options(flags: int) -> int:
-    """Tile-kernel strategy switches, a mask of TM_STREAM_ACTIVATIONS and
-    TM_WORKSPACE_SPLITK (0 = pick each strategy where it fits; see
+    """Tile-kernel strategy switches, a mask of at most one activation feed
+    (TM_STREAM_ACTIVATIONS, TM_PREQUANT_ACTIVATIONS, TM_RESIDENT_ACTIVATIONS)
+    and TM_WORKSPACE_SPLITK (0 = pick each strategy where it fits; see
     fp8gq_set_tm_options in include/fp8gq.h).  Returns the previous mask."""
     prev = load().fp8gq_set_tm_options(int(flags))
     if prev < 0:
-        raise ValueError(f"unknown tile-kernel option bits in {flags!r}")
+        raise ValueError(f"unknown or conflicting tile-kernel option bits in {flags!r}")
     return prev
 
 

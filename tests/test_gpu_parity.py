@@ -219,20 +219,25 @@ def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
     (4, 4096, 1152, False),     # 9 row blocks: a cluster of 8 per row block, one CTA per SM
     (2, 10368, 896, False),     # stream-K: CTA ranges cross row blocks, K blocks wrap
     (16, 1024, 1280, False),    # 16 tokens x 8 K blocks: a large resident footprint
-    (16, 4096, 6144, False),    # 16 tokens x 8 K blocks per CTA: resident
-    (16, 4096, 24576, False),   # 16 tokens x 32 K blocks: pre-quantised feed (B tiles by TMA)
+    (16, 4096, 6144, False),    # 16 tokens x 8 K blocks per CTA: the resident feed fits
+    (16, 4096, 24576, False),   # 16 tokens x 32 K blocks: only the pre-quantised feed fits
     (12, 12288, 4096, True),    # pre-quantised SwiGLU feed
     (40, 2048, 2560, False),    # 64-token tile
+    (6, 3072, 4096, False),     # groups of 2 K blocks, 2 idle token rows each
+    (8, 4096, 24576, False),
     (1, 12288, 4096, True),
     (2, 12288, 4096, True),
     (3, 2560, 2560, True),
 ])
 def test_tile_kernel_strategies_agree(fp8gq, cuda_device, M, K, N, swiglu):
-    """The activation feed (resident / streaming) and the split-K reduction
-    (cluster / workspace) change where data waits, not what is
-    computed: the same MMAs on the same bytes, partial sums added in the same
-    order.  All combinations agree bit for bit, with each other and (quant
-    outputs) with the oracle."""
+    """The activation feed (resident / streaming / pre-quantised) and the
+    split-K reduction (cluster / workspace) change where data waits, not what
+    is computed: the same MMAs on the same bytes, partial sums added in the
+    same order.  All combinations agree bit for bit, with each other and
+    (quant outputs) with the oracle.  The pre-quantised feed places each
+    token of an accumulator group by loading its B tile from a negative row
+    of the activation tensor; M = 1 .. 8 cover groups of 16 down to 2 K
+    blocks, non-power-of-two M included."""
     xb = gpu_activation(M, (2 * K if swiglu else K) + 64, 130 + M, cuda_device, std=1.5 if swiglu else 1.0,
                         outliers=not swiglu)
     x = xb[:, :2 * K] if swiglu else xb[:, :K]               # a row stride longer than the row
@@ -240,7 +245,9 @@ def test_tile_kernel_strategies_agree(fp8gq, cuda_device, M, K, N, swiglu):
     run = fp8gq.fused_swiglu_q_gemm if swiglu else (lambda *a, **k: fp8gq.fused_gemv_quant(*a, kernel="tm", **k))
     res = {}
     for flags in (0, fp8gq.TM_STREAM_ACTIVATIONS, fp8gq.TM_WORKSPACE_SPLITK,
-                  fp8gq.TM_STREAM_ACTIVATIONS | fp8gq.TM_WORKSPACE_SPLITK):
+                  fp8gq.TM_STREAM_ACTIVATIONS | fp8gq.TM_WORKSPACE_SPLITK,
+                  fp8gq.TM_PREQUANT_ACTIVATIONS, fp8gq.TM_PREQUANT_ACTIVATIONS | fp8gq.TM_WORKSPACE_SPLITK,
+                  fp8gq.TM_RESIDENT_ACTIVATIONS):
         prev = fp8gq.set_tm_options(flags)
         try:
             res[flags] = [t.clone() for t in run(x, wq, ws, return_quant=True)]
@@ -256,8 +263,11 @@ def test_tile_kernel_strategies_agree(fp8gq, cuda_device, M, K, N, swiglu):
 
 
 def test_tile_options_reject_unknown_bits(fp8gq, cuda_device):
-    with pytest.raises(ValueError):
-        fp8gq.set_tm_options(4)
+    for flags in (16, fp8gq.TM_STREAM_ACTIVATIONS | fp8gq.TM_PREQUANT_ACTIVATIONS,
+                  fp8gq.TM_PREQUANT_ACTIVATIONS | fp8gq.TM_RESIDENT_ACTIVATIONS):
+        with pytest.raises(ValueError):
+            fp8gq.set_tm_options(flags)
+    assert fp8gq.set_tm_options(0) == 0
 
 
 def test_tile_kernel_workspace_shared_across_shapes(fp8gq, cuda_device):
