@@ -7,9 +7,15 @@ gate_up 4096->24576, down 12288->4096 -- for each of 36 layers, every layer
 with its own seeded random e4m3 weights and 128x128 fp32 block scales
 (W ~ N(0, 0.02^2) block-quantised, activations bf16 ~ N(0, 1) with 1% of the
 channels x20).  6.95 GB of weights per step, far larger than the 126 MB L2,
-so no L2 flush is needed between steps.  With --gpus N > 1 every linear is
-sharded by output rows across the ranks and its bf16 output is all-gathered
-(NCCL) after it, so the total work is fixed (strong scaling).
+so no L2 flush is needed between steps.  With --gpus N > 1 the weights are
+sharded across the ranks, so the total work is fixed (strong scaling):
+--tp-mode paired makes qkv and gate_up column-parallel and o and
+down row-parallel, the row-parallel kernels storing their partial outputs
+into every rank's slabs over NVLink and the next column-parallel kernel
+adding them in its add + RMSNorm prologue (two exchanges per layer);
+--tp-mode gather (default) shards every linear by output rows and its kernel stores
+its slice into every rank's output; --tp-mode nccl shards the same way and
+all-gathers with NCCL after each linear.
 
 value     algorithmic bytes per step / device time per step (CUDA graph of one
           step, CUDA events, max over ranks), in GB/s (whole job).
@@ -85,9 +91,13 @@ def parse():
     ap.add_argument("--static-weights", type=int, default=0,
                     help="1: declare the weights static (fp8gq.set_static_weights), letting each "
                          "kernel prefetch its first weight tiles before the previous one finishes")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
-                    help="N > 1: the kernels store their output slices into every rank's buffer over "
-                         "NVLink (p2p, default), or an NCCL all-gather follows every linear (nccl)")
+    ap.add_argument("--tp-mode", choices=["paired", "gather", "nccl"], default="gather",
+                    help="N > 1: paired -- qkv and gate_up column-parallel, o and down "
+                         "row-parallel; each row-parallel kernel stores its partial into every rank's "
+                         "slab over NVLink and the next column-parallel kernel adds the slabs in its "
+                         "add + RMSNorm prologue (two exchanges per layer); gather (default) -- every "
+                         "linear N-sharded, the kernels store their output slices into every rank's buffer; "
+                         "nccl -- every linear N-sharded, an NCCL all-gather after each")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
@@ -254,7 +264,10 @@ def run_ours(args):
         if world > 1:
             dist.barrier()
 
-    # ---- operands: each rank owns rows [r*N/world, (r+1)*N/world) of every linear
+    paired = world > 1 and args.tp_mode == "paired"
+    # ---- operands: each rank owns rows [r*N/world, (r+1)*N/world) of every
+    # linear (gather / nccl modes), or, paired, rows of qkv and gate_up and
+    # columns [r*K/world, (r+1)*K/world) of o and down
     layers = []
     xs_len = sum(K for _, K, _ in SHAPES)
     out_len = sum(N for _, _, N in SHAPES)
@@ -267,7 +280,10 @@ def run_ours(args):
         xo = oo = so = 0
         for i, (name, K, N) in enumerate(SHAPES):
             Nr = N // world
-            wq, ws = make_weight_gpu(Nr, K, seed=100000 * L + 1000 * i + rank, dev=dev)
+            if paired and name in ("o", "down"):
+                wq, ws = make_weight_gpu(N, K // world, seed=100000 * L + 1000 * i + rank, dev=dev)
+            else:
+                wq, ws = make_weight_gpu(Nr, K, seed=100000 * L + 1000 * i + rank, dev=dev)
             x = x_all[L, xo:xo + K].view(1, K)
             xv = torch.randn(1, K, generator=g, device=dev)
             ch = torch.randperm(K, generator=g, device=dev)[: round(0.01 * K)]
@@ -282,7 +298,7 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     pg = None
-    if world > 1 and args.gather == "p2p":
+    if world > 1 and args.tp_mode == "gather":
         from fp8gq.dist import PeerGather
         pg = PeerGather(out_all.view(-1))
         # descriptors of every linear's output slice, built once (each call
@@ -290,8 +306,52 @@ def run_ours(args):
         # would for its input)
         descs = [[pg.descriptor(lin[i][6], rank * (lin[i][2] // world), True) for i in range(len(SHAPES))]
                  for lin in layers]
+    if paired:
+        # Paired tensor parallelism, layer by layer:
+        #   qkv      column-parallel, add + RMSNorm prologue over the sum of the
+        #            previous layer's down partials (layer 0: the step input)
+        #   o        row-parallel on this rank's q columns of the qkv output (the
+        #            attention output stand-in), partial -> every rank's slab
+        #   gate_up  column-parallel (gate and up rows of the rank together),
+        #            prologue sums the o partials + residual, RMSNorm
+        #   down     row-parallel, SwiGLU of the local gate_up slice, partial ->
+        #            every rank's slab
+        from fp8gq.dist import PeerGather
+        H = SHAPES[0][1]
+        slab_buf = torch.zeros(LAYERS * 2 * world * H, dtype=torch.bfloat16, device=dev)
+        pg = PeerGather(slab_buf)
+        slabs = slab_buf.view(LAYERS, 2, world, 1, H)
+        res_buf = torch.empty(LAYERS + 1, 2, 1, H, dtype=torch.bfloat16, device=dev)
+        h_in = torch.randn(1, H, generator=g, device=dev).bfloat16()
+        res_buf[0, 1].copy_(torch.randn(1, H, generator=g, device=dev).bfloat16())
+        norm_w = (torch.randn(H, generator=g, device=dev) * 0.1 + 1).bfloat16()
+        pdesc = [[pg.partial_descriptor(slabs[L, j]) for j in range(2)] for L in range(LAYERS)]
+        wdesc = pg.wait_descriptor()
+        q_cols = SHAPES[1][1] // world          # o_proj's K slice: this rank's attention heads
+
+    def paired_step():
+        for L, lin in enumerate(layers):
+            (_, _, _, wqkv, sqkv, _, _, qkv_o), (_, _, _, wo, so, _, _, _), \
+                (_, _, _, wgu, sgu, _, _, gu_o), (_, _, _, wd, sd, _, _, _) = lin
+            # residuals: layer L's qkv prologue reads res_buf[L, 1] and writes
+            # res_buf[L + 1, 0]; its gate_up prologue reads that and writes
+            # res_buf[L + 1, 1] (res_buf[0, 1] is the step's input residual)
+            if L == 0:
+                fp8gq.fused_add_rmsnorm_gemv_quant(h_in, res_buf[0, 1], norm_w, wqkv, sqkv, out=qkv_o,
+                                                   residual_out=res_buf[1, 0])
+            else:
+                pg.reduce_norm_linear(slabs[L - 1, 1], res_buf[L, 1], norm_w, wqkv, sqkv, qkv_o, res_buf[L + 1, 0],
+                                      desc=wdesc)
+            pg.linear_partial(qkv_o[:, :q_cols], wo, so, slabs[L, 0], desc=pdesc[L][0])
+            pg.reduce_norm_linear(slabs[L, 0], res_buf[L + 1, 0], norm_w, wgu, sgu, gu_o, res_buf[L + 1, 1],
+                                  desc=wdesc)
+            pg.linear_partial(gu_o, wd, sd, slabs[L, 1], swiglu=True, desc=pdesc[L][1])
+        pg.wait(slabs[LAYERS - 1, 1, rank])     # the step ends when the last partials have landed
 
     def step():
+        if paired:
+            paired_step()
+            return
         for li, lin in enumerate(layers):
             for i, (name, K, N, wq, ws, x, out, shard) in enumerate(lin):
                 if world == 1:
@@ -363,18 +423,30 @@ def run_ours(args):
         return s0.elapsed_time(s1) * 1e3 / (reps * len(calls))
 
     def per_shape(kernel):
+        """Device time per call of each shape's op on this rank's weights
+        (graph of the 36 layers' launches).  Paired: o and down are the
+        row-parallel ops on K / world columns (down with its SwiGLU prologue)."""
         res = {}
         for i, (name, K, N) in enumerate(SHAPES):
+            rowpar = paired and name in ("o", "down")
+            swiglu = paired and name == "down" and kernel == "auto"
+            Kl, Nl = (K // world, N) if rowpar else (K, N // world)
             calls = []
             for lin in layers:
                 _, _, _, wq, ws, x, out, shard = lin[i]
-                o = out if world == 1 else shard
-                calls.append(lambda x=x, wq=wq, ws=ws, o=o: fp8gq.fused_gemv_quant(x, wq, ws, out=o, kernel=kernel))
+                o = out if (world == 1 or rowpar) else shard
+                if swiglu:
+                    gu = x[:, :2 * Kl]
+                    calls.append(lambda gu=gu, wq=wq, ws=ws, o=o: fp8gq.fused_swiglu_q_gemm(gu, wq, ws, out=o))
+                else:
+                    xl = x[:, :Kl]
+                    calls.append(lambda xl=xl, wq=wq, ws=ws, o=o: fp8gq.fused_gemv_quant(xl, wq, ws, out=o,
+                                                                                         kernel=kernel))
             us = graph_us(calls)
-            b = alg_bytes(1, K, N // world)
+            b = alg_bytes(1, Kl, Nl)
             res[name] = {"us_per_call": round(us, 3), "gbs": round(b / (us * 1e-6) / 1e9, 1), "bytes_per_call": b}
             if kernel == "auto":
-                res[name]["kernel"] = ROUTED_KERNEL(N // world, K)
+                res[name]["kernel"] = ROUTED_KERNEL(Nl, Kl, swiglu=swiglu)
         return res
 
     per = per_shape("auto")
@@ -463,18 +535,26 @@ def run_ours(args):
                 "peak_source": f"{peak_kind} hbm_gbs (copy bandwidth)"}
 
     # ---- e2e: public API, eager, host buffers in and out
-    x_host = torch.empty_like(x_all, device="cpu").pin_memory()
-    x_host.copy_(x_all.cpu())
-    o_host = torch.empty_like(out_all, device="cpu").pin_memory()
+    # (paired: the step's input hidden state and residual in, the last
+    # layer's down partials and residual out; otherwise every linear's input
+    # in and every output out)
+    e2e_in = [h_in, res_buf[0, 1]] if paired else [x_all]
+    e2e_out = [slabs[LAYERS - 1, 1], res_buf[LAYERS, 1]] if paired else [out_all]
+    hosts_in = [torch.empty_like(t, device="cpu").pin_memory() for t in e2e_in]
+    for t, h in zip(e2e_in, hosts_in):
+        h.copy_(t.cpu())
+    hosts_out = [torch.empty_like(t, device="cpu").pin_memory() for t in e2e_out]
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     for it in range(3 + args.e2e_steps):
         if it == 3:
             barrier()
             torch.cuda.synchronize()
             e0.record()
-        x_all.copy_(x_host, non_blocking=True)
+        for t, h in zip(e2e_in, hosts_in):
+            t.copy_(h, non_blocking=True)
         step()
-        o_host.copy_(out_all, non_blocking=True)
+        for t, h in zip(e2e_out, hosts_out):
+            h.copy_(t, non_blocking=True)
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
@@ -483,8 +563,11 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = {"value": round(STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
-           "h2d_bytes_per_step": x_all.numel() * 2, "d2h_bytes_per_step": out_all.numel() * 2,
-           "ms_per_step": round(e2e_ms, 4), "path": "fp8gq.fused_gemv_quant (eager) per linear"}
+           "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_in),
+           "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_out),
+           "ms_per_step": round(e2e_ms, 4),
+           "path": ("fp8gq.dist.PeerGather paired linears (eager)" if paired else
+                    "fp8gq.fused_gemv_quant (eager) per linear")}
 
     torch.cuda.synchronize()
     assert fp8gq.device_error() == 0, "a kernel recorded a wait timeout"
@@ -506,8 +589,12 @@ def run_ours(args):
                 "config": {"workload": WORKLOAD, "M": 1, "layers": LAYERS,
                            "bytes_per_step": STEP_BYTES,
                            "l2": "inputs larger than L2 (6.95 GB of weights per step, 126 MB L2)",
-                           "parallelism": (f"N-sharded x{world}, output slices stored into every rank by the "
-                                           "kernels over NVLink" if pg is not None else
+                           "parallelism": ((f"paired tensor parallel x{world}: qkv, gate_up column-parallel, "
+                                            "o, down row-parallel; partials stored into every rank's slab by "
+                                            "the kernels over NVLink and summed in the next linear's add + "
+                                            "RMSNorm prologue") if paired else
+                                           (f"N-sharded x{world}, output slices stored into every rank by the "
+                                            "kernels over NVLink") if pg is not None else
                                            f"N-sharded x{world} + NCCL all-gather per linear") if world > 1
                            else "single GPU", "timing": "CUDA graph of one step, CUDA events",
                            "static_weights": bool(args.static_weights)},

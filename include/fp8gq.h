@@ -150,6 +150,8 @@ typedef struct fp8gq_gather {
     int world;                               /* 2 .. FP8GQ_MAX_GATHER_RANKS */
     int rank;
     int wait_input;
+    int local_out;                           /* 1: only wait; the output stays local
+                                                (set by the reduce entry point below) */
 } fp8gq_gather;
 
 /* fp8gq_fused_gemv_quant with the output gathered as above (routing and
@@ -163,6 +165,41 @@ int fp8gq_fused_gemv_quant_gather(const void *x, int64_t ldx, const void *w, int
  * this rank's last gathered output has arrived -- e.g. before the full output
  * is read by something that is not a gathered call with wait_input set. */
 int fp8gq_gather_wait(const fp8gq_gather *gather, fp8gq_stream_t stream);
+
+/* Tensor-parallel pairing without a gather in between: a column-parallel
+ * (N-sharded) linear keeps its output slice on its rank, where it feeds a
+ * row-parallel (K-sharded) linear whose output is a partial sum over its K
+ * slice.  Each rank stores that partial [M, N] into slab `rank` of every
+ * rank's partial buffer [world][M][N] -- an fp8gq_gather with out[r] = rank
+ * r's buffer + rank * M * N elements, col0 = 0, ldo = N -- and the next
+ * column-parallel linear adds the slabs in rank order in its prologue
+ * (fp8gq_fused_reduce_add_rmsnorm_gemv_quant).  One exchange per block
+ * (attention: qkv -> o; MLP: gate_up -> down) instead of an all-gather after
+ * every linear.  No counterpart in the reference (single-GPU).
+ *
+ * fp8gq_fused_swiglu_q_gemm with the output stored through `gather` (the
+ * row-parallel down_proj: gu is this rank's [gate | up] slice, I its width). */
+int fp8gq_fused_swiglu_q_gemm_gather(const void *gu, int64_t ldgu, const void *w, int64_t ldw,
+                                     const float *ws, int64_t ldws, int M, int N, int I,
+                                     const fp8gq_gather *gather, void *workspace, size_t workspace_bytes,
+                                     fp8gq_stream_t stream);
+
+/* fp8gq_fused_add_rmsnorm_gemv_quant (below) whose x is the sum of nsrc
+ * (1 .. FP8GQ_MAX_GATHER_RANKS) bf16 [M, K] sources src_stride elements apart,
+ * each with row stride ldx:
+ *   s = ((x_0 + x_1) + ... + x_{nsrc-1}) + residual   (fp32, left to right)
+ * then the same norm, residual_out = bf16(s), quant and GEMV into `out` on
+ * this rank.  With `wait` (a descriptor of the row-parallel calls that stored
+ * the sources; wait_input and local_out are implied, out[] is ignored) the
+ * kernel first waits, bounded, until every rank's flag has caught up.
+ * nsrc = 1 with wait = NULL is fp8gq_fused_add_rmsnorm_gemv_quant. */
+int fp8gq_fused_reduce_add_rmsnorm_gemv_quant(const void *x, int nsrc, int64_t src_stride, int64_t ldx,
+                                              const void *residual, int64_t ldr, const void *norm_w, float eps,
+                                              const void *w, int64_t ldw, const float *ws, int64_t ldws,
+                                              void *out, int64_t ldo, void *residual_out, int64_t ldro,
+                                              int M, int N, int K, uint8_t *xq_out, float *sx_out,
+                                              const fp8gq_gather *wait, void *workspace, size_t workspace_bytes,
+                                              fp8gq_stream_t stream);
 
 /* Device-memory mapping between the processes of one node (CUDA IPC).
  * fp8gq_ipc_get: a 64-byte handle of the allocation that holds `ptr`, and

@@ -320,11 +320,33 @@ def add_rmsnorm(x: np.ndarray, r: np.ndarray, w: np.ndarray, eps=RMS_EPS):
     Returns (out, residual_out, rstd) as float32 arrays ([M, K], [M, K], [M])."""
     x = np.asarray(x, np.float32)
     r = np.asarray(r, np.float32)
+    return _rmsnorm_of_sum((x + r).astype(np.float32), w, eps)
+
+
+def reduce_add_rmsnorm(partials, r: np.ndarray, w: np.ndarray, eps=RMS_EPS):
+    """add_rmsnorm whose x is the sum of the partial outputs of a K-sharded
+    (row-parallel) linear, one bf16 [M, K] array per rank, added in rank order
+    in fp32 before the residual:
+        s = ((p_0 + p_1) + ... + p_{n-1}) + r
+    (one partial: add_rmsnorm).  The reference is single-GPU; this is what an
+    all-reduce of the partials followed by its add + RMSNorm
+    (kernels/fused_rmsnorm.py:14-27) computes, with the order of the
+    additions fixed.  Returns (out, residual_out, rstd)."""
+    parts = [np.asarray(p, np.float32) for p in partials]
+    if not parts:
+        raise ValueError("at least one partial")
+    acc = parts[0]
+    for p in parts[1:]:
+        acc = (acc + p).astype(np.float32)
+    return _rmsnorm_of_sum((acc + np.asarray(r, np.float32)).astype(np.float32), w, eps)
+
+
+def _rmsnorm_of_sum(s: np.ndarray, w, eps):
+    """The norm of add_rmsnorm applied to the fp32 sum s."""
     w = np.asarray(w, np.float32)
-    M, K = x.shape
+    M, K = s.shape
     if K % GROUP:
         raise ValueError("K must be a multiple of 128")
-    s = (x + r).astype(np.float32)
     sq = (s * s).astype(np.float32).reshape(M, K // GROUP, 8, 16)
     c = np.zeros(sq.shape[:3], np.float32)
     for k in range(16):                                            # chunk sums, left to right
@@ -348,6 +370,16 @@ def fused_add_rmsnorm_gemv_quant(x, r, nw, wq, ws, eps=RMS_EPS):
     output exactly as fused_gemv_quant quantises its input.  Returns
     (out_bf16_as_f32, exact_f64, xq, sx, residual_out)."""
     h, res, _ = add_rmsnorm(x, r, nw, eps)
+    xq, sx = group_quant(h)
+    exact = gemv_from_quant(xq, sx, wq, ws)
+    return bf16_round(exact.astype(np.float32)), exact, xq, sx, res
+
+
+def fused_reduce_add_rmsnorm_gemv_quant(partials, r, nw, wq, ws, eps=RMS_EPS):
+    """fused_add_rmsnorm_gemv_quant fed by reduce_add_rmsnorm (the sum of the
+    partials in rank order, then the residual).  Returns
+    (out_bf16_as_f32, exact_f64, xq, sx, residual_out)."""
+    h, res, _ = reduce_add_rmsnorm(partials, r, nw, eps)
     xq, sx = group_quant(h)
     exact = gemv_from_quant(xq, sx, wq, ws)
     return bf16_round(exact.astype(np.float32)), exact, xq, sx, res

@@ -6,6 +6,7 @@
 #include <atomic>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/fp8gq.h"
 #include "fp8gq_device.cuh"
@@ -231,6 +232,7 @@ int to_gather_params(const fp8gq_gather* gather, GatherParams* g) {
   g->world = gather->world;
   g->rank = gather->rank;
   g->wait_input = gather->wait_input ? 1 : 0;
+  g->local_out = gather->local_out ? 1 : 0;
   return FP8GQ_OK;
 }
 
@@ -388,24 +390,52 @@ int fp8gq_add_rmsnorm(const void* x, int64_t ldx, const void* residual, int64_t 
   return launch_status();
 }
 
-int fp8gq_fused_add_rmsnorm_gemv_quant(const void* x, int64_t ldx, const void* residual, int64_t ldr,
-                                       const void* norm_w, float eps, const void* w, int64_t ldw, const float* ws,
-                                       int64_t ldws, void* out, int64_t ldo, void* residual_out, int64_t ldro,
-                                       int M, int N, int K, uint8_t* xq_out, float* sx_out, void* workspace,
-                                       size_t workspace_bytes, fp8gq_stream_t stream) {
+int fp8gq_fused_reduce_add_rmsnorm_gemv_quant(const void* x, int nsrc, int64_t src_stride, int64_t ldx,
+                                              const void* residual, int64_t ldr, const void* norm_w, float eps,
+                                              const void* w, int64_t ldw, const float* ws, int64_t ldws, void* out,
+                                              int64_t ldo, void* residual_out, int64_t ldro, int M, int N, int K,
+                                              uint8_t* xq_out, float* sx_out, const fp8gq_gather* wait,
+                                              void* workspace, size_t workspace_bytes, fp8gq_stream_t stream) {
   int st = check_common(x, w, ws, out, M, N, K, ldw, ldws, ldo);
   if (st != FP8GQ_OK) return st;
   if (!residual || !norm_w) return FP8GQ_ERR_NULL_POINTER;
+  if (nsrc < 1 || nsrc > kMaxSumSources) return FP8GQ_ERR_SHAPE;
   if (ldx < K || ldr < K || (residual_out && ldro < K)) return FP8GQ_ERR_STRIDE;
+  // the sources must not overlap one another's rows
+  if (nsrc > 1 && src_stride < static_cast<int64_t>(M - 1) * ldx + K) return FP8GQ_ERR_STRIDE;
   const uintptr_t mis = reinterpret_cast<uintptr_t>(residual) | reinterpret_cast<uintptr_t>(norm_w) |
                         reinterpret_cast<uintptr_t>(residual_out);
-  if ((mis & 15u) || (ldx % 8) || (ldr % 8) || (residual_out && (ldro % 8))) return FP8GQ_ERR_ALIGNMENT;
+  if ((mis & 15u) || (ldx % 8) || (ldr % 8) || (residual_out && (ldro % 8)) || (nsrc > 1 && src_stride % 8))
+    return FP8GQ_ERR_ALIGNMENT;
   if (residual_out) {
-    // CTA 0 writes residual_out while other CTAs still read residual
-    const uintptr_t r0 = reinterpret_cast<uintptr_t>(residual), o0 = reinterpret_cast<uintptr_t>(residual_out);
-    const uintptr_t r1 = r0 + static_cast<uintptr_t>((static_cast<int64_t>(M - 1) * ldr + K) * 2);
-    const uintptr_t o1 = o0 + static_cast<uintptr_t>((static_cast<int64_t>(M - 1) * ldro + K) * 2);
-    if (r0 < o1 && o0 < r1) return FP8GQ_ERR_UNSUPPORTED;
+    // CTA 0 writes residual_out while other CTAs still read the residual and
+    // the sources
+    auto span = [](const void* p, int64_t elems) {
+      const uintptr_t b = reinterpret_cast<uintptr_t>(p);
+      return std::make_pair(b, b + static_cast<uintptr_t>(elems * 2));
+    };
+    const auto o = span(residual_out, static_cast<int64_t>(M - 1) * ldro + K);
+    const auto r = span(residual, static_cast<int64_t>(M - 1) * ldr + K);
+    const auto xs = span(x, static_cast<int64_t>(nsrc - 1) * src_stride + static_cast<int64_t>(M - 1) * ldx + K);
+    if ((r.first < o.second && o.first < r.second) || (xs.first < o.second && o.first < xs.second))
+      return FP8GQ_ERR_UNSUPPORTED;
+  }
+  GatherParams g{};
+  if (wait) {
+    // only the input wait: flags, seq, world and rank of the descriptor
+    if (!wait->seq) return FP8GQ_ERR_NULL_POINTER;
+    if (wait->world < 2 || wait->world > FP8GQ_MAX_GATHER_RANKS || wait->rank < 0 || wait->rank >= wait->world)
+      return FP8GQ_ERR_SHAPE;
+    for (int q = 0; q < wait->world; ++q) {
+      if (!wait->flags[q]) return FP8GQ_ERR_NULL_POINTER;
+      if (reinterpret_cast<uintptr_t>(wait->flags[q]) & 3u) return FP8GQ_ERR_ALIGNMENT;
+      g.flags[q] = wait->flags[q];
+    }
+    g.seq = wait->seq;
+    g.world = wait->world;
+    g.rank = wait->rank;
+    g.wait_input = 1;
+    g.local_out = 1;
   }
   NormParams nrm{};
   nrm.res = static_cast<const __nv_bfloat16*>(residual);
@@ -415,14 +445,27 @@ int fp8gq_fused_add_rmsnorm_gemv_quant(const void* x, int64_t ldx, const void* r
   nrm.ldro = ldro;
   nrm.eps = eps;
   nrm.norm = 1;
+  nrm.nsrc = nsrc;
+  nrm.src_stride = src_stride;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (M == 1 && m1_uses_row(N, K)) return launch_row(false, x, w, ldw, ws, ldws, out, N, K, xq_out, sx_out, s, nullptr, &nrm);
+  const GatherParams* gp = wait ? &g : nullptr;
+  if (M == 1 && m1_uses_row(N, K)) return launch_row(false, x, w, ldw, ws, ldws, out, N, K, xq_out, sx_out, s, gp, &nrm);
   DeviceInfo di;
   st = device_info(&di, nullptr);
   if (st != FP8GQ_OK) return st;
   return launch_tm(false, x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace, workspace_bytes,
                    di.sm_count, di.max_smem_optin, s, g_static_weights.load(std::memory_order_relaxed), 0,
-                   1, tm_cluster_mode(), nullptr, &nrm);
+                   1, tm_cluster_mode(), gp, &nrm);
+}
+
+int fp8gq_fused_add_rmsnorm_gemv_quant(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                                       const void* norm_w, float eps, const void* w, int64_t ldw, const float* ws,
+                                       int64_t ldws, void* out, int64_t ldo, void* residual_out, int64_t ldro,
+                                       int M, int N, int K, uint8_t* xq_out, float* sx_out, void* workspace,
+                                       size_t workspace_bytes, fp8gq_stream_t stream) {
+  return fp8gq_fused_reduce_add_rmsnorm_gemv_quant(x, 1, 0, ldx, residual, ldr, norm_w, eps, w, ldw, ws, ldws, out,
+                                                   ldo, residual_out, ldro, M, N, K, xq_out, sx_out, nullptr,
+                                                   workspace, workspace_bytes, stream);
 }
 
 int fp8gq_fused_gemv_quant_gather(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
@@ -443,6 +486,28 @@ int fp8gq_fused_gemv_quant_gather(const void* x, int64_t ldx, const void* w, int
   st = device_info(&di, nullptr);
   if (st != FP8GQ_OK) return st;
   return launch_tm(false, x, ldx, w, ldw, ws, ldws, own, gather->ldo, M, N, K, nullptr, nullptr, workspace,
+                   workspace_bytes, di.sm_count, di.max_smem_optin, s, g_static_weights.load(std::memory_order_relaxed),
+                   0, tm_resident_mode(), tm_cluster_mode(), &g);
+}
+
+int fp8gq_fused_swiglu_q_gemm_gather(const void* gu, int64_t ldgu, const void* w, int64_t ldw, const float* ws,
+                                     int64_t ldws, int M, int N, int I, const fp8gq_gather* gather,
+                                     void* workspace, size_t workspace_bytes, fp8gq_stream_t stream) {
+  GatherParams g;
+  int st = to_gather_params(gather, &g);
+  if (st != FP8GQ_OK) return st;
+  if (gather->ldo < static_cast<int64_t>(gather->col0) + N) return FP8GQ_ERR_STRIDE;
+  void* own = static_cast<__nv_bfloat16*>(gather->out[gather->rank]) + gather->col0;
+  st = check_common(gu, w, ws, own, M, N, I, ldw, ldws, gather->ldo);
+  if (st != FP8GQ_OK) return st;
+  if (ldgu < 2 * static_cast<int64_t>(I)) return FP8GQ_ERR_STRIDE;
+  if (ldgu % 8) return FP8GQ_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 1 && m1_uses_row(N, I)) return launch_row(true, gu, w, ldw, ws, ldws, own, N, I, nullptr, nullptr, s, &g);
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  return launch_tm(true, gu, ldgu, w, ldw, ws, ldws, own, gather->ldo, M, N, I, nullptr, nullptr, workspace,
                    workspace_bytes, di.sm_count, di.max_smem_optin, s, g_static_weights.load(std::memory_order_relaxed),
                    0, tm_resident_mode(), tm_cluster_mode(), &g);
 }

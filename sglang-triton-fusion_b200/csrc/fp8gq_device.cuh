@@ -239,6 +239,8 @@ __device__ __forceinline__ float octet_sum(float c) {
   return c;
 }
 
+constexpr int kMaxSumSources = 8;    // partial outputs summed by the reduce prologue (one per rank)
+
 __device__ __forceinline__ float rms_rstd(float ssq, int K, float eps) {
   const float var = __fdiv_rn(ssq, static_cast<float>(K));
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
@@ -252,6 +254,44 @@ __device__ __forceinline__ void add16(float (&s)[16], uint4 xa, uint4 xb, uint4 
   for (int e = 0; e < 8; ++e) {
     s[2 * e] = __fadd_rn(bf16_lo(xw[e]), bf16_lo(rw[e]));
     s[2 * e + 1] = __fadd_rn(bf16_hi(xw[e]), bf16_hi(rw[e]));
+  }
+}
+
+// 16 values s = ((x_0 + x_1) + ... + x_{n-1}) + r, added left to right in
+// fp32: n >= 1 bf16 sources `stride` elements apart (the partial outputs of a
+// K-sharded linear, one per rank, in rank order), then the residual.  With
+// n == 1 it is add16's single addition.  L2-coherent loads: the sources may
+// have been stored into this GPU's memory by other GPUs.
+__device__ __forceinline__ void addn16(float (&s)[16], const __nv_bfloat16* x, int64_t stride, int n,
+                                       const __nv_bfloat16* r) {
+  const uint4* x0 = reinterpret_cast<const uint4*>(x);
+  const uint4 a0 = __ldcg(x0), b0 = __ldcg(x0 + 1);
+  const uint32_t w0[8] = {a0.x, a0.y, a0.z, a0.w, b0.x, b0.y, b0.z, b0.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    s[2 * e] = bf16_lo(w0[e]);
+    s[2 * e + 1] = bf16_hi(w0[e]);
+  }
+#pragma unroll
+  for (int i = 1; i < kMaxSumSources; ++i) {
+    if (i < n) {
+      const uint4* xi = reinterpret_cast<const uint4*>(x + i * stride);
+      const uint4 a = __ldcg(xi), b = __ldcg(xi + 1);
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        s[2 * e] = __fadd_rn(s[2 * e], bf16_lo(w[e]));
+        s[2 * e + 1] = __fadd_rn(s[2 * e + 1], bf16_hi(w[e]));
+      }
+    }
+  }
+  const uint4* rp = reinterpret_cast<const uint4*>(r);
+  const uint4 ra = __ldcg(rp), rb = __ldcg(rp + 1);
+  const uint32_t rw[8] = {ra.x, ra.y, ra.z, ra.w, rb.x, rb.y, rb.z, rb.w};
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    s[2 * e] = __fadd_rn(s[2 * e], bf16_lo(rw[e]));
+    s[2 * e + 1] = __fadd_rn(s[2 * e + 1], bf16_hi(rw[e]));
   }
 }
 
@@ -278,14 +318,17 @@ __device__ __forceinline__ void pack_bf16x16(const float (&s)[16], uint4& a, uin
   b = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-// Parameters of the add + RMSNorm prologue (norm = 0: none).
+// Parameters of the add + RMSNorm prologue (norm = 0: none).  The activation
+// x may be the sum of nsrc sources (x, x + src_stride, ...), see addn16.
 struct NormParams {
   const __nv_bfloat16* res;   // residual [M, ldr]
   const __nv_bfloat16* w;     // norm weight [K]
-  __nv_bfloat16* res_out;     // x + residual [M, ldro], written once (by CTA 0)
+  __nv_bfloat16* res_out;     // sum + residual [M, ldro], written once (by CTA 0)
   int64_t ldr, ldro;
   float eps;
   int norm;
+  int nsrc;                   // sources summed into x (0 or 1: x alone)
+  int64_t src_stride;         // elements from one source to the next
 };
 
 // ---------------------------------------------------------------------------
@@ -301,6 +344,12 @@ constexpr int kMaxGatherRanks = 8;
 // reached this rank's sequence number, i.e. after every slice of the last
 // gathered output has landed here.  All ranks run the same sequence of
 // gathered kernels, so their sequence numbers advance together.
+//
+// A K-sharded (row-parallel) linear uses the same stores for its partial
+// output: out[r] points at this rank's slab in rank r's buffer of per-rank
+// partials, col0 = 0.  A kernel with local_out set only waits (wait_input) and
+// writes its own output locally, publishing nothing: the column-parallel
+// linear that reduces those partials in its prologue.
 struct GatherParams {
   __nv_bfloat16* out[kMaxGatherRanks];   // rank r's full output [M, ldo], as mapped here
   unsigned int* flags[kMaxGatherRanks];  // rank r's flags[world], as mapped here
@@ -311,7 +360,11 @@ struct GatherParams {
   int world;                             // 0: no gather (plain local output)
   int rank;
   int wait_input;
+  int local_out;                         // 1: output to the local `out` only, no flags raised
 };
+
+// Whether a kernel's output goes to every rank (and raises the flags).
+__device__ __forceinline__ bool gather_publishes(const GatherParams& g) { return g.world > 0 && !g.local_out; }
 
 __device__ __forceinline__ unsigned int ld_acquire_sys_u32(const unsigned int* p) {
   unsigned int v;

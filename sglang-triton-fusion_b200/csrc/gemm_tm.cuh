@@ -404,7 +404,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // sx ring (a plain shared-memory flag; the epilogue polls it)
   volatile uint32_t* sx_tag = reinterpret_cast<volatile uint32_t*>(tmem_empty + kTmMaxAcc);
   uint64_t* drain = tmem_empty + kTmMaxAcc + kTmSxRing;  // MMA completion on the error path
-  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag, [2] input wait failed
+  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag
   // streaming: [kTmSxRing][MT] ring indexed by j; resident: [slot][M]
   float* sx_ring = reinterpret_cast<float*>(misc + 4);
   float* ws_cache = sx_ring + kTmSxRing * MT;          // [min(J, kTmWsCache)]
@@ -440,7 +440,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   const int kb0 = static_cast<int>(u0 - static_cast<int64_t>(nb0) * p.KB);
   // output element (token m, column n of this launch): local, or to every rank
   auto store_out = [&](int m, int n, __nv_bfloat16 v) {
-    if (p.gather.world > 0)
+    if (gather_publishes(p.gather))
       gather_store(p.gather, m, n, v);
     else
       p.out[static_cast<int64_t>(m) * p.ldo + n] = v;
@@ -460,10 +460,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       mbar_init(&acc_full[lane], 1);     // tcgen05.commit
       mbar_init(&tmem_empty[lane], 4);   // 4 epilogue warps
     }
-    if (lane == 0) {
-      mbar_init(drain, 1);
-      misc[2] = 0u;
-    }
+    if (lane == 0) mbar_init(drain, 1);
     for (int r = lane; r < kTmSxRing; r += 32) sx_tag[r] = 0u;
     fence_mbar_init();
   } else if (warp == 1) {
@@ -508,10 +505,24 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   }
   grid_dependency_wait();
   if (p.gather.wait_input) {
-    // the activation is a gathered output: every rank's slice must be here
-    if (warp == 0 && !gather_wait_input(p.gather, lane) && lane == 0) misc[2] = 1u;
-    __syncthreads();
-    if (misc[2]) ok = false;
+    // The activation comes from other ranks: the warps that read it wait for
+    // every rank's flag -- warps 2-9, and with the streaming feed the TMA warp
+    // too (it loads the activation tiles).  Otherwise warps 0 and 1 start the
+    // weight stream and the MMA loop at once: the flags cover the activation,
+    // not the weights, and the MMAs wait for B tiles built after this wait.
+    // (The pre-quantised feed is never chosen for such a launch: its quant
+    // kernel would read the activation before the wait.)  A wait that gives
+    // up has recorded the error word; the kernel then runs to its end on
+    // whatever the activation holds (as the row kernel does), so every role
+    // keeps its normal path.
+    const bool tma_reads_x = !resident && !prequant;
+    if (tma_reads_x || warp >= 2) {
+      if (warp == 2) gather_wait_input(p.gather, lane);
+      if (tma_reads_x)
+        __syncthreads();
+      else
+        named_bar_sync(1, kTmThreads - 64);
+    }
   }
   // Warps 0 and 1 start their loops at once; warps 2-9 first finish the block
   // scales and, resident, quantise the CTA's K range (8 warps x 4 lane octets,
@@ -566,7 +577,9 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
         }
       };
       if (!kSwiglu && p.norm.norm) {
-        // add + RMSNorm: every CTA first sums the squares of the whole rows
+        // (reduce +) add + RMSNorm: x is the sum of p.norm.nsrc sources in
+        // source order (the partials of a K-sharded linear), then + residual.
+        // Every CTA first sums the squares of the whole rows
         // (all K blocks, not only its own) -- chunk sums, octet sums per
         // 128-group into norm_sum[m][b] -- and one thread per token adds the
         // groups in order
@@ -579,10 +592,8 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           const int b = live ? g - m * p.KB : 0;
           float sv[16];
           if (live) {
-            const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + b * 128 + chunk * 16);
-            const uint4* rr =
-                reinterpret_cast<const uint4*>(p.norm.res + static_cast<int64_t>(m) * p.norm.ldr + b * 128 + chunk * 16);
-            add16(sv, __ldcg(xr), __ldcg(xr + 1), __ldcg(rr), __ldcg(rr + 1));
+            addn16(sv, p.x + static_cast<int64_t>(m) * p.ldx + b * 128 + chunk * 16, p.norm.src_stride, p.norm.nsrc,
+                   p.norm.res + static_cast<int64_t>(m) * p.norm.ldr + b * 128 + chunk * 16);
           } else {
 #pragma unroll
             for (int e = 0; e < 16; ++e) sv[e] = 0.0f;
@@ -614,12 +625,10 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           if (live) group_of(g, m, r, kb);
           float v[16];
           if (live) {
-            const uint4* xr = reinterpret_cast<const uint4*>(p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 + chunk * 16);
-            const uint4* rr =
-                reinterpret_cast<const uint4*>(p.norm.res + static_cast<int64_t>(m) * p.norm.ldr + kb * 128 + chunk * 16);
             const uint4* wr = reinterpret_cast<const uint4*>(p.norm.w + kb * 128 + chunk * 16);
             float sv[16];
-            add16(sv, __ldcg(xr), __ldcg(xr + 1), __ldcg(rr), __ldcg(rr + 1));
+            addn16(sv, p.x + static_cast<int64_t>(m) * p.ldx + kb * 128 + chunk * 16, p.norm.src_stride, p.norm.nsrc,
+                   p.norm.res + static_cast<int64_t>(m) * p.norm.ldr + kb * 128 + chunk * 16);
             norm16(v, sv, gsum[p.M * p.KB + m], __ldg(wr), __ldg(wr + 1));
           } else {
 #pragma unroll
@@ -1081,7 +1090,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 
   tc_fence_before();
   __syncthreads();
-  if (p.gather.world > 0 && tid == 0) gather_cta_done(p.gather, gridDim.x);
+  if (gather_publishes(p.gather) && tid == 0) gather_cta_done(p.gather, gridDim.x);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
@@ -1436,11 +1445,12 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   const int64_t xcols = swiglu ? 2 * static_cast<int64_t>(K) : K;
   // Pre-quantised feed: large M whose activation does not stay resident at
   // this grid -- quantise it once here (into xq_out / sx_out when given, else
-  // the workspace) instead of in every CTA.
+  // the workspace) instead of in every CTA.  Not for a launch that waits for
+  // other ranks' activation (the quant kernel would read it before the wait).
   bool pre = false;
   uint8_t* pre_xq = nullptr;
   float* pre_sx = nullptr;
-  if (resident_mode != 0 && tm_prequant_shape(M) && !(norm && norm->norm)) {
+  if (resident_mode != 0 && tm_prequant_shape(M) && !(norm && norm->norm) && !(gather && gather->wait_input)) {
     const int mp0 = M < MT ? M : MT;
     TmPlan pl0;
     bool ok0;
@@ -1495,7 +1505,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     }
     if (gather) {
       // this pass's rows of every rank's output; only the first pass waits
-      for (int r = 0; r < gather->world; ++r) p.gather.out[r] = gather->out[r] + static_cast<int64_t>(m0) * gather->ldo;
+      if (!gather->local_out)
+        for (int r = 0; r < gather->world; ++r) p.gather.out[r] = gather->out[r] + static_cast<int64_t>(m0) * gather->ldo;
       if (m0 > 0) p.gather.wait_input = 0;
     }
     p.xq_out = (xq_out && !pre) ? xq_out + static_cast<int64_t>(m0) * K : nullptr;

@@ -203,8 +203,9 @@ gemv_row_kernel(const RowParams p) {
   // Quantise this thread's chunks of the activation (whole 128-groups are
   // shared by 8 consecutive lanes, so the group amax is a 3-step shuffle).
   const int n_chunks = p.K / 16;
-  // add + RMSNorm: first the row's sum of squares (chunk sums, octet sums per
-  // 128-group into shared memory, then one thread adds the groups in order)
+  // (reduce +) add + RMSNorm: first the row's sum of squares (chunk sums, octet
+  // sums per 128-group into shared memory, then one thread adds the groups in
+  // order); x is the sum of p.norm.nsrc sources, see addn16
   float rstd = 0.0f;
   if (!kSwiglu && p.norm.norm) {
     float* gsum = window;                 // [K/128 + 1] until the main loop
@@ -214,9 +215,7 @@ gemv_row_kernel(const RowParams p) {
       const bool valid = c < n_chunks;
       float sv[16];
       if (valid) {
-        const uint4* xp = reinterpret_cast<const uint4*>(p.x + 16 * c);
-        const uint4* rp = reinterpret_cast<const uint4*>(p.norm.res + 16 * c);
-        add16(sv, xp[0], xp[1], rp[0], rp[1]);
+        addn16(sv, p.x + 16 * c, p.norm.src_stride, p.norm.nsrc, p.norm.res + 16 * c);
       } else {
 #pragma unroll
         for (int e = 0; e < 16; ++e) sv[e] = 0.0f;
@@ -262,15 +261,14 @@ gemv_row_kernel(const RowParams p) {
           v[2 * e + 1] = silu_mul(bf16_hi(gw[e]), bf16_hi(uw[e]));
         }
       } else {
-        const uint4* xp = reinterpret_cast<const uint4*>(p.x + 16 * c);
-        const uint4 a = xp[0], b = xp[1];
         if (p.norm.norm) {
-          const uint4* rp = reinterpret_cast<const uint4*>(p.norm.res + 16 * c);
           const uint4* wp = reinterpret_cast<const uint4*>(p.norm.w + 16 * c);
           float sv[16];
-          add16(sv, a, b, rp[0], rp[1]);
+          addn16(sv, p.x + 16 * c, p.norm.src_stride, p.norm.nsrc, p.norm.res + 16 * c);
           norm16(v, sv, rstd, wp[0], wp[1]);
         } else {
+          const uint4* xp = reinterpret_cast<const uint4*>(p.x + 16 * c);
+          const uint4 a = xp[0], b = xp[1];
           const uint32_t xw[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
@@ -367,7 +365,7 @@ gemv_row_kernel(const RowParams p) {
           float sum = 0.0f;
           for (int w = 0; w < n_cwarps; ++w) sum += win[w * kRowWindow + lane];
           const __nv_bfloat16 v = __float2bfloat16_rn(sum);
-          if (p.gather.world > 0)
+          if (gather_publishes(p.gather))
             gather_store(p.gather, 0, row_begin + wrow0 + lane, v);
           else
             p.out[row_begin + wrow0 + lane] = v;
@@ -378,7 +376,7 @@ gemv_row_kernel(const RowParams p) {
   }
   (void)rows_my;
   (void)in_ok;
-  if (p.gather.world > 0) {
+  if (gather_publishes(p.gather)) {
     named_bar_sync(1, T);   // every output store of this CTA is issued
     if (tid == 0) gather_cta_done(p.gather, gridDim.x);
   }

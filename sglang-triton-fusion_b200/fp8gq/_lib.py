@@ -40,7 +40,8 @@ class Gather(ctypes.Structure):
                 ("col0", ctypes.c_int),
                 ("world", ctypes.c_int),
                 ("rank", ctypes.c_int),
-                ("wait_input", ctypes.c_int)]
+                ("wait_input", ctypes.c_int),
+                ("local_out", ctypes.c_int)]
 
 
 # name -> (restype, argtypes); the order of include/fp8gq.h
@@ -65,6 +66,11 @@ SIGNATURES = {
     "fp8gq_fused_gemv_quant_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
                                            _P, _SZ, _P]),
     "fp8gq_gather_wait": (_I, [ctypes.POINTER(Gather), _P]),
+    "fp8gq_fused_swiglu_q_gemm_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
+                                              _P, _SZ, _P]),
+    "fp8gq_fused_reduce_add_rmsnorm_gemv_quant": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, ctypes.c_float, _P, _I64,
+                                                       _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P,
+                                                       ctypes.POINTER(Gather), _P, _SZ, _P]),
     "fp8gq_ipc_get": (_I, [_P, _P, ctypes.POINTER(ctypes.c_uint64)]),
     "fp8gq_ipc_open": (_I, [_P, ctypes.c_uint64, ctypes.POINTER(_P), ctypes.POINTER(_P)]),
     "fp8gq_ipc_close": (_I, [_P]),

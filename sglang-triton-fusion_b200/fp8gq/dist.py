@@ -12,6 +12,15 @@ Two ways to gather:
   * PeerGather: the kernel itself stores its slice into every rank's output
     buffer over NVLink (peer memory mapped with CUDA IPC) and raises a flag;
     the next gathered call waits for the flags inside its kernel.
+
+Paired tensor parallelism (no gather between two linears): a column-parallel
+linear (rows sharded as above; shard_gate_up keeps each rank's gate and up rows
+together) leaves its slice on its rank, where it is the input of a row-parallel
+linear (shard_cols: the K columns sharded) whose output is a partial sum.
+PeerGather.linear_partial stores that partial into every rank's slab of a
+[world, M, N] buffer, and PeerGather.reduce_norm_linear -- the next
+column-parallel linear -- adds the slabs in rank order in its add + RMSNorm
+prologue after waiting for every rank.
 """
 from __future__ import annotations
 
@@ -32,6 +41,33 @@ def shard_rows(Wq: torch.Tensor, Ws: torch.Tensor, rank: int, world: int):
     per = nb // world
     return (Wq[rank * per * ops.GROUP:(rank + 1) * per * ops.GROUP],
             Ws[rank * per:(rank + 1) * per])
+
+
+def shard_cols(Wq: torch.Tensor, Ws: torch.Tensor, rank: int, world: int):
+    """Rank `rank`'s K slice of a weight [N, K] (columns, whole 128-column
+    blocks) and of its block scales [N/128, K/128]: the row-parallel half of a
+    pair, whose output is a partial sum over the slice."""
+    K = Wq.shape[1]
+    kb = K // ops.GROUP
+    if K % ops.GROUP or kb % world:
+        raise ops.ShapeError(f"K/128 = {kb} column blocks do not split evenly over {world} ranks")
+    per = kb // world
+    return (Wq[:, rank * per * ops.GROUP:(rank + 1) * per * ops.GROUP],
+            Ws[:, rank * per:(rank + 1) * per])
+
+
+def shard_gate_up(Wq: torch.Tensor, Ws: torch.Tensor, rank: int, world: int):
+    """Rank `rank`'s rows of a merged [gate; up] weight [2I, K]: its slice of
+    the gate rows followed by the same slice of the up rows (contiguous copies),
+    so that its output is the [gate | up] input of a SwiGLU over its I/world
+    intermediate columns."""
+    I2 = Wq.shape[0]
+    if I2 % 2:
+        raise ops.ShapeError("the merged gate/up weight needs an even row count")
+    I = I2 // 2
+    gq, gs = shard_rows(Wq[:I], Ws[:I // ops.GROUP], rank, world)
+    uq, us = shard_rows(Wq[I:], Ws[I // ops.GROUP:], rank, world)
+    return torch.cat([gq, uq]).contiguous(), torch.cat([gs, us]).contiguous()
 
 
 def all_gather_columns(shard: torch.Tensor, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
@@ -150,6 +186,67 @@ class PeerGather:
             0 if ws_buf is None else ws_buf.numel(), ops._stream(x.device))
         _lib.check(st, "fp8gq_fused_gemv_quant_gather")
         return out
+
+    def partial_descriptor(self, slabs: torch.Tensor) -> "_lib.Gather":
+        """The struct fp8gq_gather that stores this rank's [M, N] partial into
+        slab `rank` of ``slabs`` -- a [world, M, N] view into ``buffer`` -- on
+        every rank."""
+        if slabs.dim() != 3 or slabs.shape[0] != self.world or not slabs.is_contiguous():
+            raise ValueError("slabs must be a contiguous [world, M, N] view into the PeerGather buffer")
+        g = self.descriptor(slabs[self.rank], 0, False)
+        off = slabs.data_ptr() - self.buffer.data_ptr() + self.rank * slabs.stride(0) * 2
+        for r in range(self.world):
+            g.out[r] = self.buf_ptrs[r] + off
+        return g
+
+    def wait_descriptor(self) -> "_lib.Gather":
+        """A descriptor that only waits for every rank's last publishing call."""
+        g = _lib.Gather()
+        for r in range(self.world):
+            g.flags[r] = self.flag_ptrs[r]
+        g.counter = self.state.data_ptr()
+        g.seq = self.state.data_ptr() + 4
+        g.ldo = 1
+        g.world = self.world
+        g.rank = self.rank
+        g.wait_input = 1
+        g.local_out = 1
+        return g
+
+    def linear_partial(self, x: torch.Tensor, Wq_cols: torch.Tensor, Ws_cols: torch.Tensor, slabs: torch.Tensor,
+                       swiglu: bool = False, desc=None):
+        """The row-parallel half of a pair: this rank's partial output
+        x @ Wq_cols^T (K slice; with swiglu, x is this rank's [gate | up]
+        slice) stored into slab `rank` of ``slabs`` on every rank."""
+        M = x.shape[0]
+        N, Kr = Wq_cols.shape
+        if slabs.shape[1:] != (M, N):
+            raise ops.ShapeError(f"slabs must be [{self.world}, {M}, {N}], got {tuple(slabs.shape)}")
+        if swiglu:
+            if x.shape[1] != 2 * Kr:
+                raise ops.ShapeError(f"gu must be [M, {2 * Kr}], got {tuple(x.shape)}")
+        elif x.shape[1] != Kr:
+            raise ops.ShapeError(f"x must be [M, {Kr}], got {tuple(x.shape)}")
+        ops._check_weight(Wq_cols, Ws_cols, Kr)
+        g = desc if desc is not None else self.partial_descriptor(slabs)
+        nbytes = self.lib.fp8gq_workspace_bytes(M, N, Kr)
+        ws_buf = ops.workspace(x.device, nbytes) if nbytes else None
+        fn = self.lib.fp8gq_fused_swiglu_q_gemm_gather if swiglu else self.lib.fp8gq_fused_gemv_quant_gather
+        st = fn(x.data_ptr(), x.stride(0), Wq_cols.data_ptr(), Wq_cols.stride(0), Ws_cols.data_ptr(),
+                Ws_cols.stride(0), M, N, Kr, ctypes.byref(g), None if ws_buf is None else ws_buf.data_ptr(),
+                0 if ws_buf is None else ws_buf.numel(), ops._stream(x.device))
+        _lib.check(st, "fp8gq_fused_swiglu_q_gemm_gather" if swiglu else "fp8gq_fused_gemv_quant_gather")
+        return slabs
+
+    def reduce_norm_linear(self, slabs: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor,
+                           Wq_rows: torch.Tensor, Ws_rows: torch.Tensor, out: torch.Tensor,
+                           residual_out: torch.Tensor, eps: float = ops.RMS_EPS, desc=None):
+        """The next column-parallel linear: waits for every rank's partial,
+        then out = GEMV(quant(rmsnorm(sum of slabs in rank order + residual)))
+        on this rank's rows; residual_out = bf16(sum + residual)."""
+        g = desc if desc is not None else self.wait_descriptor()
+        return ops.fused_reduce_add_rmsnorm_gemv_quant(slabs, residual, norm_weight, Wq_rows, Ws_rows, eps,
+                                                       out=out, residual_out=residual_out, wait=g)
 
     def wait(self, out: torch.Tensor):
         """Enqueue a wait for the last gathered call's slices from every rank."""

@@ -268,3 +268,36 @@ def fused_add_rmsnorm_gemv_quant(x: torch.Tensor, residual: torch.Tensor, norm_w
         M, N, K, _ptr(xq), _ptr(sx), _ptr(ws_buf), 0 if ws_buf is None else ws_buf.numel(), _stream(x.device))
     _lib.check(st, "fp8gq_fused_add_rmsnorm_gemv_quant")
     return (out, residual_out, xq, sx) if return_quant else (out, residual_out)
+
+
+def fused_reduce_add_rmsnorm_gemv_quant(partials: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor,
+                                        Wq: torch.Tensor, Ws: torch.Tensor, eps: float = RMS_EPS, *, out=None,
+                                        residual_out=None, return_quant: bool = False, wait=None):
+    """fused_add_rmsnorm_gemv_quant whose x is the sum of the partial outputs
+    of a K-sharded linear: ``partials`` is [S, M, K] bf16 (S <= 8 slabs, one per
+    rank, any slab stride, rows contiguous), added in slab order in fp32 before
+    the residual.  ``wait`` (an fp8gq._lib.Gather of the calls that stored the
+    slabs) makes the kernel wait for every rank first.  Returns (out,
+    residual_out) or, with return_quant, (out, residual_out, xq, sx)."""
+    if partials.dim() != 3:
+        raise ShapeError("partials must be [S, M, K]")
+    S = partials.shape[0]
+    if not 1 <= S <= _lib.MAX_GATHER_RANKS:
+        raise ShapeError(f"1 .. {_lib.MAX_GATHER_RANKS} partial slabs, got {S}")
+    M, K = _check_norm_inputs(partials[0], residual, norm_weight)
+    N = _check_weight(Wq, Ws, K)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=partials.device)
+    if residual_out is None:
+        residual_out = torch.empty(M, K, dtype=torch.bfloat16, device=partials.device)
+    xq, sx = _quant_out(M, K, partials.device, return_quant)
+    lib = _lib.load()
+    nbytes = lib.fp8gq_workspace_bytes(M, N, K)
+    ws_buf = workspace(partials.device, nbytes) if nbytes else None
+    st = lib.fp8gq_fused_reduce_add_rmsnorm_gemv_quant(
+        _ptr(partials), S, partials.stride(0), partials.stride(1), _ptr(residual), residual.stride(0),
+        _ptr(norm_weight), float(eps), _ptr(Wq), Wq.stride(0), _ptr(Ws), Ws.stride(0), _ptr(out), out.stride(0),
+        _ptr(residual_out), residual_out.stride(0), M, N, K, _ptr(xq), _ptr(sx), wait,
+        _ptr(ws_buf), 0 if ws_buf is None else ws_buf.numel(), _stream(partials.device))
+    _lib.check(st, "fp8gq_fused_reduce_add_rmsnorm_gemv_quant")
+    return (out, residual_out, xq, sx) if return_quant else (out, residual_out)

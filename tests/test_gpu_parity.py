@@ -383,6 +383,54 @@ def test_add_rmsnorm_stress_battery(fp8gq, cuda_device):
         fp8gq.fused_add_rmsnorm_gemv_quant(x, r, ones, wq, ws, residual_out=r)
 
 
+# ------------------- reduce + add + RMSNorm prologue (paired tensor parallel) --
+
+@pytest.mark.parametrize("M, K, N, S, gap", [
+    (1, 4096, 6144, 3, 0),      # tile kernel, three partial slabs back to back
+    (1, 4096, 4096, 8, 256),    # row kernel, eight slabs with a gap between them
+    (1, 4096, 3072, 2, 0),      # row kernel: the gate_up slice of a rank at 8-way tensor parallel
+    (4, 4096, 24576, 5, 128),   # tile kernel, M = 4
+    (16, 2560, 4096, 8, 0),
+])
+def test_fused_reduce_add_rmsnorm_gemv(fp8gq, cuda_device, M, K, N, S, gap):
+    """x = the sum of S partial slabs in slab order, then + residual: residual
+    output and quantised bytes bit-exact against the oracle, output within
+    the GEMV tolerance."""
+    store = torch.zeros(S, M * K + gap, dtype=torch.bfloat16, device=cuda_device)
+    parts = store[:, :M * K].view(S, M, K)
+    for i in range(S):
+        parts[i].copy_(gpu_activation(M, K, 800 + 10 * i + M, cuda_device, std=0.5))
+    _, r, w = _norm_inputs(M, K, 850 + M, cuda_device)
+    wq, ws = gpu_weight(N, K, 851, cuda_device)
+    out, res, xq, sx = fp8gq.fused_reduce_add_rmsnorm_gemv_quant(parts, r, w, wq, ws, return_quant=True)
+    _, exact, rq, rs, rres = O.fused_reduce_add_rmsnorm_gemv_quant([to_f32(parts[i]) for i in range(S)], to_f32(r),
+                                                                   to_f32(w), to_u8(wq), to_f32(ws))
+    assert np.array_equal(to_f32(res), rres)
+    assert np.array_equal(to_u8(xq), rq) and np.array_equal(to_f32(sx), rs)
+    assert_close(to_f32(out), exact, 3.0)
+
+
+def test_fused_reduce_one_slab_is_add_rmsnorm(fp8gq, cuda_device):
+    """One slab is the plain fused add + RMSNorm, bit for bit."""
+    x, r, w = _norm_inputs(1, 4096, 860, cuda_device)
+    wq, ws = gpu_weight(6144, 4096, 861, cuda_device)
+    a = fp8gq.fused_add_rmsnorm_gemv_quant(x, r, w, wq, ws, return_quant=True)
+    b = fp8gq.fused_reduce_add_rmsnorm_gemv_quant(x.unsqueeze(0), r, w, wq, ws, return_quant=True)
+    for u, v in zip(a, b):
+        assert torch.equal(u, v)
+
+
+def test_fused_reduce_rejects_bad_slabs(fp8gq, cuda_device):
+    K = 4096
+    parts = gpu_activation(9, K, 870, cuda_device).view(9, 1, K)
+    _, r, w = _norm_inputs(1, K, 871, cuda_device)
+    wq, ws = gpu_weight(4096, K, 872, cuda_device)
+    with pytest.raises(fp8gq.ShapeError):                 # more slabs than ranks
+        fp8gq.fused_reduce_add_rmsnorm_gemv_quant(parts, r, w, wq, ws)
+    with pytest.raises(fp8gq.Fp8gqError):                 # residual_out may not alias a slab
+        fp8gq.fused_reduce_add_rmsnorm_gemv_quant(parts[:2], r, w, wq, ws, residual_out=parts[1])
+
+
 # ---------------------------------------- stand-alone SwiGLU writers --
 
 @pytest.mark.parametrize("M, I", [(512, 9728), (16, 9728), (3, 256), (1, 12288)])

@@ -98,3 +98,129 @@ def test_peer_gather_matches_per_rank_ops():
         assert p.exitcode == 0
     for rank, errs in results.items():
         assert not errs, f"rank {rank}: {errs}"
+
+
+def _paired_worker(rank, world, port, result_q):
+    """One MLP block of paired tensor parallelism: row-parallel o_proj stores
+    its partial into every rank's slab, column-parallel gate_up reduces the
+    slabs in its add + RMSNorm prologue, the SwiGLU + down_proj partials go
+    to the second set of slabs, and a second reduce + norm linear sums them."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "sglang-triton-fusion_b200")]
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import fp8gq
+    from fp8gq import dist as fdist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+    try:
+        fp8gq.load()
+        errs = []
+        H, I, NQ = 4096, 6144, 6144
+        for M in (1, 4):
+            buf = torch.zeros(2 * world * M * H + 64, dtype=torch.bfloat16, device=dev)
+            pg = fdist.PeerGather(buf, group=None)
+            slabs_o = buf[:world * M * H].view(world, M, H)
+            slabs_d = buf[world * M * H:2 * world * M * H].view(world, M, H)
+            g = torch.Generator(device=dev).manual_seed(40 + M)
+            a = (torch.randn(M, H, generator=g, device=dev)).bfloat16()
+            res0 = (torch.randn(M, H, generator=g, device=dev)).bfloat16()
+            nw = (torch.randn(H, generator=g, device=dev) * 0.1 + 1).bfloat16()
+            wo, so = _weight(H, H, 41, dev)
+            wgu, sgu = _weight(2 * I, H, 42, dev)
+            wd, sd = _weight(H, I, 43, dev)
+            wq, sq = _weight(NQ, H, 44, dev)
+            kr = H // world
+            wo_r, so_r = fdist.shard_cols(wo, so, rank, world)
+            wgu_r, sgu_r = fdist.shard_gate_up(wgu, sgu, rank, world)
+            wd_r, sd_r = fdist.shard_cols(wd, sd, rank, world)
+            wq_r, sq_r = fdist.shard_rows(wq, sq, rank, world)
+            a_r = a[:, rank * kr:(rank + 1) * kr]
+            gu_r = torch.empty(M, wgu_r.shape[0], dtype=torch.bfloat16, device=dev)
+            res1 = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+            q_r = torch.empty(M, wq_r.shape[0], dtype=torch.bfloat16, device=dev)
+            res2 = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+            pg.linear_partial(a_r, wo_r, so_r, slabs_o)
+            pg.reduce_norm_linear(slabs_o, res0, nw, wgu_r, sgu_r, gu_r, res1)
+            pg.linear_partial(gu_r, wd_r, sd_r, slabs_d, swiglu=True)
+            pg.reduce_norm_linear(slabs_d, res1, nw, wq_r, sq_r, q_r, res2)
+            torch.cuda.synchronize()
+            # the same steps as local single-GPU calls on the landed slabs
+            po = fp8gq.fused_gemv_quant(a_r, wo_r, so_r)
+            pd = fp8gq.fused_swiglu_q_gemm(gu_r, wd_r, sd_r)
+            all_po = [torch.empty_like(po) for _ in range(world)]
+            all_pd = [torch.empty_like(pd) for _ in range(world)]
+            dist.all_gather(all_po, po)
+            dist.all_gather(all_pd, pd)
+            for q in range(world):
+                if not torch.equal(slabs_o[q], all_po[q]):
+                    errs.append(f"M={M}: o slab {q} != rank {q}'s partial")
+                if not torch.equal(slabs_d[q], all_pd[q]):
+                    errs.append(f"M={M}: down slab {q} != rank {q}'s partial")
+            gu2, r1 = fp8gq.fused_reduce_add_rmsnorm_gemv_quant(slabs_o.clone(), res0, nw, wgu_r, sgu_r)
+            q2, r2 = fp8gq.fused_reduce_add_rmsnorm_gemv_quant(slabs_d.clone(), res1, nw, wq_r, sq_r)
+            if not (torch.equal(gu2, gu_r) and torch.equal(r1, res1)):
+                errs.append(f"M={M}: waiting gate_up reduce != local reduce")
+            if not (torch.equal(q2, q_r) and torch.equal(r2, res2)):
+                errs.append(f"M={M}: waiting second reduce != local reduce")
+            # each stage against the unsharded op on the same inputs (the
+            # K-split and the bf16 partials change only the rounding), the
+            # reduce exactly, and the whole block against the unsharded chain
+            # loosely (there a few e4m3 codes differ and travel down the chain)
+            def rel(x, y):
+                return ((x.float() - y.float()).norm() / y.float().norm()).item()
+            Ir = I // world
+            gu_all = [torch.empty_like(gu_r) for _ in range(world)]
+            dist.all_gather(gu_all, gu_r)
+            gu_joined = torch.cat([g_[:, :Ir] for g_ in gu_all] + [g_[:, Ir:] for g_ in gu_all], 1)
+            gu_one, _ = fp8gq.fused_reduce_add_rmsnorm_gemv_quant(slabs_o.clone(), res0, nw, wgu, sgu)
+            gu_one_r = torch.cat([gu_one[:, rank * Ir:(rank + 1) * Ir], gu_one[:, I + rank * Ir:I + (rank + 1) * Ir]], 1)
+            checks = {"sum of o partials": rel(slabs_o.float().sum(0), fp8gq.fused_gemv_quant(a, wo, so)),
+                      "gate_up slice": rel(gu_r, gu_one_r),
+                      "sum of down partials": rel(slabs_d.float().sum(0), fp8gq.fused_swiglu_q_gemm(gu_joined, wd, sd))}
+            for name, v in checks.items():
+                if not v <= 1e-2:
+                    errs.append(f"M={M}: {name} differs from the unsharded op: relative L2 {v:.4g}")
+            acc = slabs_d[0].float()
+            for q in range(1, world):
+                acc = acc + slabs_d[q].float()
+            if not torch.equal(res2, (acc + res1.float()).bfloat16()):
+                errs.append(f"M={M}: residual 2 != bf16(sum of down partials in rank order + residual 1)")
+            o_full = fp8gq.fused_gemv_quant(a, wo, so)
+            gu_full, r1f = fp8gq.fused_add_rmsnorm_gemv_quant(o_full, res0, nw, wgu, sgu)
+            d_full = fp8gq.fused_swiglu_q_gemm(gu_full, wd, sd)
+            _, r2f = fp8gq.fused_add_rmsnorm_gemv_quant(d_full, r1f, nw, wq, sq)
+            if not rel(res2, r2f) <= 5e-2:
+                errs.append(f"M={M}: the block's residual differs from the unsharded chain: {rel(res2, r2f):.4g}")
+            if fp8gq.device_error() != 0:
+                errs.append(f"device error word {fp8gq.device_error():#x}")
+            pg.close()
+        result_q.put((rank, errs))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_paired_tensor_parallel_block():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    world = 2
+    port = _free_port()
+    procs = [ctx.Process(target=_paired_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, errs = q.get(timeout=300)
+        results[rank] = errs
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, errs in results.items():
+        assert not errs, f"rank {rank}: {errs}"

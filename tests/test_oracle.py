@@ -240,3 +240,46 @@ def test_make_weight_block_quant():
     blk = np.abs(O.E4M3_TABLE[wq]).reshape(2, 128, 3, 128).max(axis=(1, 3))
     assert np.all(blk == 448.0)
     assert np.all(np.isfinite(deq))
+
+
+def test_reduce_add_rmsnorm_one_partial_is_add_rmsnorm():
+    rng = np.random.default_rng(3)
+    x = O.bf16_round(rng.standard_normal((2, 512)).astype(np.float32))
+    r = O.bf16_round(rng.standard_normal((2, 512)).astype(np.float32))
+    w = O.bf16_round((rng.standard_normal(512) * 0.1 + 1).astype(np.float32))
+    for a, b in zip(O.add_rmsnorm(x, r, w), O.reduce_add_rmsnorm([x], r, w)):
+        assert np.array_equal(a, b)
+
+
+def test_reduce_add_rmsnorm_adds_in_rank_order():
+    """((p0 + p1) + p2) + r, left to right: with p0 = 2^26, p1 = -2^26, p2 = 1
+    the sum is 1 (right to left it would round to 0)."""
+    K = 128
+    p0 = np.full((1, K), 2.0 ** 26, np.float32)
+    p1 = -p0
+    p2 = np.ones((1, K), np.float32)
+    r = np.full((1, K), 0.5, np.float32)
+    w = np.ones(K, np.float32)
+    _, res, _ = O.reduce_add_rmsnorm([p0, p1, p2], r, w)
+    assert np.all(res == np.float32(1.5))
+    assert np.float32(p0[0, 0] + np.float32(p1[0, 0] + p2[0, 0])) + np.float32(0.5) == np.float32(0.5)
+
+
+def test_k_sharded_partials_sum_to_the_full_gemv():
+    """A K-sharded linear's partials (each rank quantises its own 128-groups,
+    which are the full activation's groups) add up to the unsharded GEMV
+    within the GEMV tolerance."""
+    M, K, N, world = 2, 1024, 512, 4
+    x = O.make_activation(M, K, seed=11)
+    wq, ws = O.make_weight(N, K, seed=12)
+    _, full, _, _ = O.fused_gemv_quant(x, wq, ws)
+    kr = K // world
+    parts = []
+    for r in range(world):
+        out, _, _, _ = O.fused_gemv_quant(x[:, r * kr:(r + 1) * kr], wq[:, r * kr:(r + 1) * kr],
+                                          ws[:, r * kr // 128:(r + 1) * kr // 128])
+        parts.append(out)
+    acc = parts[0]
+    for p in parts[1:]:
+        acc = (acc + p).astype(np.float32)
+    assert O.north_star_ok(acc, full)
