@@ -101,7 +101,9 @@ def parse():
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
-                         "or 'stack' for the whole decode step's routed linears")
+                         "norm_<shape> (add + RMSNorm prologue), writer, add_rmsnorm, group_quant "
+                         "(activation kernels alone, M rows), or 'stack' for the whole decode step's "
+                         "routed linears")
     return ap.parse_args()
 
 
@@ -241,6 +243,58 @@ def make_weight_gpu(N, K, seed, dev):
     ws = blk.abs().amax(dim=(1, 3)).clamp_min(1e-10) / 448.0
     q = (blk / ws[:, None, :, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(N, K)
     return q.contiguous(), ws.contiguous()
+
+
+def decode_chain(layers, dev, M=1):
+    """The decode step as a chain over the stack's weights: qkv -> o (the
+    first 4096 columns of qkv's output, an attention stand-in) -> gate_up ->
+    down (SwiGLU of gate_up's output) -> the next layer's qkv, every input the
+    previous linear's output.  Returns (fp8gq.Linear list, step input)."""
+    import torch
+    import fp8gq
+    H = SHAPES[0][1]
+    h = torch.randn(M, H, device=dev).bfloat16()
+    x = h
+    lins = []
+    for lin in layers:
+        (_, _, Nq, wqkv, sqkv, _, _, _), (_, _, _, wo, so, _, _, _), \
+            (_, _, Ngu, wgu, sgu, _, _, _), (_, _, Nd, wd, sd, _, _, _) = lin
+        qkv = torch.empty(M, Nq, dtype=torch.bfloat16, device=dev)
+        o = torch.empty(M, H, dtype=torch.bfloat16, device=dev)
+        gu = torch.empty(M, Ngu, dtype=torch.bfloat16, device=dev)
+        d = torch.empty(M, Nd, dtype=torch.bfloat16, device=dev)
+        lins += [fp8gq.Linear(x, wqkv, sqkv, qkv), fp8gq.Linear(qkv[:, :H], wo, so, o),
+                 fp8gq.Linear(o, wgu, sgu, gu), fp8gq.Linear(gu, wd, sd, d, swiglu=True)]
+        x = d
+    return lins, h
+
+
+def stack_runner_line(layers, dev, graph_us):
+    """The decode chain as one persistent launch (fp8gq.StackRunner) against
+    the same chain as 144 routed per-linear launches (CUDA graph of each)."""
+    import torch
+    import fp8gq
+    lins, _ = decode_chain(layers, dev)
+    runner = fp8gq.StackRunner(lins)
+    runner.run()
+
+    def per_linear():
+        for lin in lins:
+            if lin.swiglu:
+                fp8gq.fused_swiglu_q_gemm(lin.x, lin.w, lin.ws, out=lin.out)
+            else:
+                fp8gq.fused_gemv_quant(lin.x, lin.w, lin.ws, out=lin.out)
+    per_linear()
+    torch.cuda.synchronize()
+    b = STEP_BYTES + LAYERS * 2 * 12288        # the SwiGLU input of down is [gate | up]
+    us_stack = graph_us([runner.run], reps=100)
+    us_lin = graph_us([per_linear], reps=100)
+    assert fp8gq.device_error() == 0, "a kernel recorded a wait timeout"
+    return {"us_per_step": round(us_stack, 2), "gbs": round(b / (us_stack * 1e-6) / 1e9, 1),
+            "per_linear_launches_us_per_step": round(us_lin, 2),
+            "per_linear_launches_gbs": round(b / (us_lin * 1e-6) / 1e9, 1), "bytes_per_step": b,
+            "linears": len(lins), "launches_per_step": 1,
+            "kernel": "stack_kernel (persistent, cooperative, one CTA per SM)"}
 
 
 def run_ours(args):
@@ -455,6 +509,8 @@ def run_ours(args):
 
     extra = {}
     if world == 1:
+        extra["stack_runner"] = stack_runner_line(layers, dev, graph_us)
+    if world == 1:
         # fused SwiGLU + quant + down_proj at M = 1 (gate_up output 24576 -> 4096)
         gus = [(torch.randn(1, 24576, device=dev) * 1.5).bfloat16() for _ in range(4)]
         calls = [lambda lin=lin, gu=gus[i % 4]: fp8gq.fused_swiglu_q_gemm(gu, lin[3][3], lin[3][4], out=lin[3][6])
@@ -631,6 +687,26 @@ def run_profile_case(args):
         print(json.dumps({"profile_case": "stack", "launches": (args.warmup + args.steps) * len(lin),
                           "bytes_per_step": STEP_BYTES}))
         return
+    if args.profile_case.startswith("stack_runner"):
+        # the decode chain of L layers (default 4: 772 MB of weights, > L2)
+        # as one persistent launch per step
+        nl = int(args.profile_case.split("L=")[1]) if "L=" in args.profile_case else 4
+        layers = []
+        for L in range(nl):
+            lin = []
+            for i, (name, K, N) in enumerate(SHAPES):
+                wq, ws = make_weight_gpu(N, K, seed=100000 * L + 1000 * i, dev=dev)
+                lin.append((name, K, N, wq, ws, None, None, None))
+            layers.append(lin)
+        lins, _ = decode_chain(layers, dev)
+        runner = fp8gq.StackRunner(lins)
+        for _ in range(args.warmup + args.steps):
+            runner.run()
+        torch.cuda.synchronize()
+        assert fp8gq.device_error() == 0
+        print(json.dumps({"profile_case": args.profile_case, "launches": args.warmup + args.steps,
+                          "bytes_per_launch": nl * sum(alg_bytes(1, K, N) for _, K, N in SHAPES) + nl * 2 * 12288}))
+        return
     parts = args.profile_case.split(":")
     shape, kernel, M = parts[0], "auto", 1
     for p in parts[1:]:
@@ -638,12 +714,46 @@ def run_profile_case(args):
             M = int(p[2:])
         else:
             kernel = p
+    g = torch.Generator(device=dev).manual_seed(2)
+    if shape in ("writer", "add_rmsnorm", "group_quant"):
+        # the activation-side kernels on their own, M rows of Qwen3-8B widths
+        # (writer: intermediate 12288, the others: hidden 4096)
+        if shape == "writer":
+            gu = torch.randn(M, 2 * 12288, generator=g, device=dev).bfloat16()
+            gate, up = gu[:, :12288], gu[:, 12288:]
+            fn = lambda: fp8gq.fused_swiglu_quant(gate, up)  # noqa: E731
+            nbytes = M * 12288 * (4 + 1) + 4 * M * 96
+        elif shape == "add_rmsnorm":
+            h = torch.randn(M, 4096, generator=g, device=dev).bfloat16()
+            r = torch.randn(M, 4096, generator=g, device=dev).bfloat16()
+            nw = (torch.randn(4096, generator=g, device=dev) * 0.1 + 1).bfloat16()
+            o, ro = torch.empty_like(h), torch.empty_like(h)
+            fn = lambda: fp8gq.add_rmsnorm(h, r, nw, out=o, residual_out=ro)  # noqa: E731
+            nbytes = M * 4096 * 2 * 4 + 4096 * 2
+        else:
+            h = torch.randn(M, 4096, generator=g, device=dev).bfloat16()
+            fn = lambda: fp8gq.group_quant(h)  # noqa: E731
+            nbytes = M * 4096 * (2 + 1) + 4 * M * 32
+        for _ in range(args.warmup + args.steps):
+            fn()
+        torch.cuda.synchronize()
+        assert fp8gq.device_error() == 0
+        print(json.dumps({"profile_case": args.profile_case, "launches": args.warmup + args.steps,
+                          "bytes_per_launch": nbytes}))
+        return
     dims = {n: (K, N) for n, K, N in SHAPES}
     dims["swiglu_down"] = (12288, 4096)
+    if shape.startswith("norm_"):
+        dims[shape] = dims[shape[5:]]
     K, N = dims[shape]
     wq, ws = make_weight_gpu(N, K, seed=1, dev=dev)
-    g = torch.Generator(device=dev).manual_seed(2)
-    if shape == "swiglu_down":
+    if shape.startswith("norm_"):
+        # add + RMSNorm as the prologue of the linear
+        h = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        r = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        nw = (torch.randn(K, generator=g, device=dev) * 0.1 + 1).bfloat16()
+        fn = lambda: fp8gq.fused_add_rmsnorm_gemv_quant(h, r, nw, wq, ws)  # noqa: E731
+    elif shape == "swiglu_down":
         x = (torch.randn(M, 2 * K, generator=g, device=dev) * 1.5).bfloat16()
         fn = lambda: fp8gq.fused_swiglu_q_gemm(x, wq, ws)  # noqa: E731
     else:

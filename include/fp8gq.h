@@ -302,6 +302,69 @@ int fp8gq_set_tm_options(int flags);
  * no error was recorded. */
 int fp8gq_device_error(uint32_t *code, int clear);
 
+/* Stack runner: a list of block-FP8 linears -- e.g. the qkv, o, gate_up and
+ * down (SwiGLU) linears of every layer of a decode step -- run in list order
+ * by ONE persistent, cooperative launch on all SMs.  Each linear is the tile
+ * kernel's fused quant + GEMM (the arithmetic of
+ * kernels/fused_gemv_quant_tm.py:49-80, and with swiglu set of
+ * kernels/fused_swiglu_quant_gemv.py:26-51); its input may be the output of
+ * an earlier linear of the list.  Every SM's TMA stream runs on into the
+ * next linear's weights while that linear waits for its input, so the
+ * per-launch gap of a linear-at-a-time decode step disappears.  A decoder
+ * that owns its step calls it once per step.  The reference has no
+ * counterpart: it launches one Triton kernel per linear.
+ *
+ * Per linear: x bf16 [M, K] (swiglu: [M, 2K] = [gate | up], act =
+ * silu(gate) * up quantised as in fp8gq_fused_swiglu_q_gemm), w e4m3 [N, K],
+ * ws fp32 [N/128, K/128], out bf16 [M, N]; K, N multiples of 128,
+ * N <= 524288; x 16-byte aligned with ldx a multiple of 8 elements; all
+ * linears share M, 1 <= M <= 16.  Linear l reads x only after every earlier
+ * linear whose output overlaps x, or whose x or out overlaps l's out, has
+ * been stored completely (fp8gq_stack_dependencies shows the choice); there
+ * is no other ordering between linears. */
+typedef struct fp8gq_stack_linear {
+    const void *x;   int64_t ldx;
+    const void *w;   int64_t ldw;
+    const float *ws; int64_t ldws;
+    void *out;       int64_t ldo;
+    int N, K;
+    int swiglu;      /* 1: x is [gate | up] with 2K columns */
+    int reserved;    /* 0 */
+} fp8gq_stack_linear;
+
+/* Host-side record of a prepared list (filled by fp8gq_stack_prepare). */
+typedef struct fp8gq_stack_plan {
+    void *device;          /* the caller's device memory holding the plan */
+    size_t bytes;
+    int n, M, device_id, grid, stages, npw;
+    int sw, lg_sw, kpb, nacc;
+    size_t smem;
+    int64_t reserved[4];
+} fp8gq_stack_plan;
+
+/* Device bytes a plan of n linears at M tokens needs on the current device
+ * (the linear table, counters and the split-K partial sums). */
+size_t fp8gq_stack_plan_bytes(int n, int M);
+
+/* For each linear, the index of the earlier linear it waits for (-1: none):
+ * the latest one whose output overlaps this linear's input, or whose input
+ * or output overlaps this linear's output.  Host only; no GPU needed. */
+int fp8gq_stack_dependencies(const fp8gq_stack_linear *lin, int n, int M, int *dep);
+
+/* Validates the list, writes the plan into `device_mem` (bytes >=
+ * fp8gq_stack_plan_bytes(n, M), 256-byte aligned) with copies on `stream`
+ * (from pageable host memory: not for use during stream capture) and fills
+ * *plan.  The plan holds the linears' pointers: re-prepare after any of them
+ * changes. */
+int fp8gq_stack_prepare(const fp8gq_stack_linear *lin, int n, int M, void *device_mem, size_t bytes,
+                        fp8gq_stack_plan *plan, fp8gq_stream_t stream);
+
+/* Runs every linear of a prepared plan: one kernel launch (capturable in a
+ * CUDA graph).  Runs that share a plan must not overlap on the GPU.  If a
+ * run records a device error (fp8gq_device_error), its outputs are invalid
+ * and the plan must be prepared again. */
+int fp8gq_stack_run(const fp8gq_stack_plan *plan, fp8gq_stream_t stream);
+
 /* fp8gq_gemv_quant_tm without a workspace argument.  No counterpart in the
  * reference (its Triton kernels need no scratch).
  *

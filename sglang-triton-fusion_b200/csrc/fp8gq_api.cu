@@ -7,6 +7,7 @@
 #include <cstring>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "../../include/fp8gq.h"
 #include "fp8gq_device.cuh"
@@ -15,6 +16,7 @@
 #include "quant_only.cuh"
 #include "swiglu_writer.cuh"
 #include "add_rmsnorm.cuh"
+#include "stack.cuh"
 
 using namespace fp8gq;
 
@@ -591,6 +593,194 @@ int fp8gq_device_error(uint32_t* code, int clear) {
     if (cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
   }
   return FP8GQ_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Stack runner (stack.cuh): plan preparation and launch.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Byte range [lo, hi) an [M, cols] bf16 operand with row stride ld covers.
+struct ByteRange {
+  uintptr_t lo, hi;
+};
+ByteRange bf16_range(const void* p, int M, int64_t cols, int64_t ld) {
+  const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
+  return {lo, lo + static_cast<uintptr_t>(((M - 1) * ld + cols) * 2)};
+}
+bool overlaps(ByteRange a, ByteRange b) { return a.lo < b.hi && b.lo < a.hi; }
+
+int stack_check(const fp8gq_stack_linear* lin, int n, int M) {
+  if (!lin) return FP8GQ_ERR_NULL_POINTER;
+  if (n < 1 || n > kStMaxLinears || M < 1 || M > kStMT) return FP8GQ_ERR_SHAPE;
+  for (int l = 0; l < n; ++l) {
+    const fp8gq_stack_linear& L = lin[l];
+    int st = check_common(L.x, L.w, L.ws, L.out, M, L.N, L.K, L.ldw, L.ldws, L.ldo);
+    if (st != FP8GQ_OK) return st;
+    const int64_t cols = L.swiglu ? 2 * static_cast<int64_t>(L.K) : L.K;
+    if (L.ldx < cols) return FP8GQ_ERR_STRIDE;
+    if (L.ldx % 8) return FP8GQ_ERR_ALIGNMENT;
+    if (L.N / kGroup > kStMaxRowBlocks) return FP8GQ_ERR_UNSUPPORTED;
+    if (L.reserved != 0 || (L.swiglu != 0 && L.swiglu != 1)) return FP8GQ_ERR_UNSUPPORTED;
+  }
+  return FP8GQ_OK;
+}
+
+void stack_deps(const fp8gq_stack_linear* lin, int n, int M, int* dep) {
+  for (int l = 0; l < n; ++l) {
+    const fp8gq_stack_linear& L = lin[l];
+    const ByteRange xl = bf16_range(L.x, M, L.swiglu ? 2 * static_cast<int64_t>(L.K) : L.K, L.ldx);
+    const ByteRange ol = bf16_range(L.out, M, L.N, L.ldo);
+    dep[l] = -1;
+    for (int i = l - 1; i >= 0; --i) {
+      const fp8gq_stack_linear& P = lin[i];
+      const ByteRange xi = bf16_range(P.x, M, P.swiglu ? 2 * static_cast<int64_t>(P.K) : P.K, P.ldx);
+      const ByteRange oi = bf16_range(P.out, M, P.N, P.ldo);
+      if (overlaps(xl, oi) || overlaps(ol, xi) || overlaps(ol, oi)) {
+        dep[l] = i;
+        break;
+      }
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fp8gq_stack_plan_bytes(int n, int M) {
+  DeviceInfo di;
+  if (n < 1 || n > kStMaxLinears || M < 1 || M > kStMT || device_info(&di, nullptr) != FP8GQ_OK) return 0;
+  return st_plan_bytes(n, M, di.sm_count);
+}
+
+int fp8gq_stack_dependencies(const fp8gq_stack_linear* lin, int n, int M, int* dep) {
+  if (!dep) return FP8GQ_ERR_NULL_POINTER;
+  const int st = stack_check(lin, n, M);
+  if (st != FP8GQ_OK) return st;
+  stack_deps(lin, n, M, dep);
+  return FP8GQ_OK;
+}
+
+int fp8gq_stack_prepare(const fp8gq_stack_linear* lin, int n, int M, void* device_mem, size_t bytes,
+                        fp8gq_stack_plan* plan, fp8gq_stream_t stream) {
+  if (!plan || !device_mem) return FP8GQ_ERR_NULL_POINTER;
+  int st = stack_check(lin, n, M);
+  if (st != FP8GQ_OK) return st;
+  DeviceInfo di;
+  int dev = 0;
+  st = device_info(&di, &dev);
+  if (st != FP8GQ_OK) return st;
+  const int G = di.sm_count;
+  if (bytes < st_plan_bytes(n, M, G) || (reinterpret_cast<uintptr_t>(device_mem) & 255u))
+    return FP8GQ_ERR_WORKSPACE;
+  // ring depth from the shared memory one CTA per SM may use
+  const int64_t avail = static_cast<int64_t>(di.max_smem_optin) - static_cast<int64_t>(kStTailBytes) - 1024;
+  const int S = st_pick_stages(avail / (kTmATileBytes + kStBTileBytes));
+  if (S < 4) return FP8GQ_ERR_UNSUPPORTED;
+  std::vector<int> dep(n);
+  stack_deps(lin, n, M, dep.data());
+  std::vector<StackLinear> table(n);
+  for (int l = 0; l < n; ++l) {
+    const fp8gq_stack_linear& L = lin[l];
+    StackLinear& T = table[l];
+    std::memset(&T, 0, sizeof(T));
+    if (!make_weight_tmap(&T.tmap_w, L.w, L.N, L.K, L.ldw)) return FP8GQ_ERR_LAUNCH;
+    T.ws = L.ws;
+    T.x = static_cast<const __nv_bfloat16*>(L.x);
+    T.out = static_cast<__nv_bfloat16*>(L.out);
+    T.ldws = L.ldws;
+    T.ldx = L.ldx;
+    T.ldo = L.ldo;
+    T.N = L.N;
+    T.K = L.K;
+    T.KB = L.K / kGroup;
+    T.U = static_cast<int64_t>(L.N / kGroup) * T.KB;
+    T.swiglu = L.swiglu;
+    T.dep = dep[l];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(device_mem);
+  if (cudaMemcpyAsync(base, table.data(), static_cast<size_t>(n) * sizeof(StackLinear), cudaMemcpyHostToDevice,
+                      s) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  // done counters, the exit counter and the split counters start at zero
+  if (cudaMemsetAsync(base + st_table_bytes(n), 0, st_done_bytes(n) + st_counter_bytes(), s) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  std::memset(plan, 0, sizeof(*plan));
+  plan->device = device_mem;
+  plan->bytes = bytes;
+  plan->n = n;
+  plan->M = M;
+  plan->device_id = dev;
+  plan->grid = G;
+  plan->stages = S;
+  plan->npw = tm_producer_warps(S);
+  int sw = 1, lg = 0;
+  while (sw < M) {
+    sw <<= 1;
+    ++lg;
+  }
+  plan->sw = sw;
+  plan->lg_sw = lg;
+  plan->kpb = kStMT / sw;
+  plan->nacc = plan->kpb >= 8 ? 2 : kTmMaxAcc;
+  plan->smem = static_cast<size_t>(S) * (kTmATileBytes + kStBTileBytes) + kStTailBytes + 1024;
+  return FP8GQ_OK;
+}
+
+int fp8gq_stack_run(const fp8gq_stack_plan* plan, fp8gq_stream_t stream) {
+  if (!plan || !plan->device) return FP8GQ_ERR_NULL_POINTER;
+  DeviceInfo di;
+  int dev = 0;
+  int st = device_info(&di, &dev);
+  if (st != FP8GQ_OK) return st;
+  if (dev != plan->device_id || plan->grid != di.sm_count) return FP8GQ_ERR_DEVICE;
+  if (plan->n < 1 || plan->n > kStMaxLinears || plan->M < 1 || plan->M > kStMT || plan->stages < 4 ||
+      plan->stages > kStMaxStages || plan->smem > static_cast<size_t>(di.max_smem_optin))
+    return FP8GQ_ERR_UNSUPPORTED;
+  uint8_t* base = static_cast<uint8_t*>(plan->device);
+  const int n = plan->n;
+  StackParams p;
+  p.lin = reinterpret_cast<const StackLinear*>(base);
+  p.done = reinterpret_cast<unsigned int*>(base + st_table_bytes(n));
+  p.exit_count = p.done + n;
+  p.counters = reinterpret_cast<int*>(base + st_table_bytes(n) + st_done_bytes(n));
+  p.partials = reinterpret_cast<float*>(base + st_table_bytes(n) + st_done_bytes(n) + st_counter_bytes());
+  p.n = n;
+  p.M = plan->M;
+  p.sw = plan->sw;
+  p.lg_sw = plan->lg_sw;
+  p.kpb = plan->kpb;
+  p.nacc = plan->nacc;
+  p.stages = plan->stages;
+  p.npw = plan->npw;
+  p.b_off = static_cast<uint32_t>(plan->stages * kTmATileBytes);
+  p.bar_off = p.b_off + static_cast<uint32_t>(plan->stages * kStBTileBytes);
+  if (cudaFuncSetAttribute(stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(plan->smem)) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  // every CTA must be resident at once (they wait for one another): one CTA
+  // per SM, launched as a cooperative grid, which the runtime refuses rather
+  // than run partly
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel, kStThreads, plan->smem) != cudaSuccess ||
+      per_sm < 1)
+    return FP8GQ_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kStThreads);
+  cfg.dynamicSmemBytes = plan->smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, stack_kernel, p) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  return launch_status();
 }
 
 }  // extern "C"

@@ -31,6 +31,8 @@ enum ErrorSite : unsigned int {
   kSiteTmTmem = 6,
   kSiteTmFixup = 7,      // tile kernel split-K partial-sum hand-off
   kSiteGather = 8,       // waiting for the peers' output slices of a gathered linear
+  kSiteStackRing = 9,    // stack runner: a ring, accumulator or scale wait inside a CTA
+  kSiteStackDep = 10,    // stack runner: waiting for every CTA to finish an earlier linear
 };
 
 __device__ __forceinline__ void record_error(unsigned int site) {

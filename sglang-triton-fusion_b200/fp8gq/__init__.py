@@ -9,6 +9,7 @@ Entry points:
   fused_swiglu(g, u), fused_swiglu_quant(g, u)   stand-alone SwiGLU writers (large M)
   add_rmsnorm(x, r, w), fused_add_rmsnorm_gemv_quant(x, r, w, Wq, Ws)   add + RMSNorm (prologue)
   fused_reduce_add_rmsnorm_gemv_quant(partials, r, w, Wq, Ws)          + the sum of K-sharded partials
+  StackRunner([Linear(x, Wq, Ws, out, swiglu)...])   a list of linears in one persistent launch
   patch_fp8_fused_tail             the sglang linear wrappers and install()
 The C ABI is include/fp8gq.h (libfp8gq.so next to this file).
 """
@@ -18,10 +19,11 @@ from .ops import (GROUP, TM, ShapeError, add_rmsnorm, fused_add_rmsnorm_gemv_qua
                   fused_reduce_add_rmsnorm_gemv_quant,
                   fused_gemv_quant, fused_swiglu, fused_swiglu_q_gemm, fused_swiglu_quant, group_quant,
                   swiglu_group_quant, workspace)
+from .stack import Linear, StackRunner  # noqa: F401
 
 __all__ = ["Fp8gqError", "ShapeError", "GROUP", "TM", "fused_gemv_quant", "fused_swiglu_q_gemm",
            "fused_swiglu", "fused_swiglu_quant", "add_rmsnorm", "fused_add_rmsnorm_gemv_quant",
            "fused_reduce_add_rmsnorm_gemv_quant",
            "group_quant", "swiglu_group_quant", "workspace", "load", "device_error", "set_static_weights",
            "set_tm_options", "TM_STREAM_ACTIVATIONS", "TM_WORKSPACE_SPLITK",
-           "TM_PREQUANT_ACTIVATIONS", "TM_RESIDENT_ACTIVATIONS"]
+           "TM_PREQUANT_ACTIVATIONS", "TM_RESIDENT_ACTIVATIONS", "Linear", "StackRunner"]

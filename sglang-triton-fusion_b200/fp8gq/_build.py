@@ -14,7 +14,8 @@ SRC_DIR = PKG_DIR.parent / "csrc"
 REPO_DIR = PKG_DIR.parent.parent
 LIB_PATH = PKG_DIR / "libfp8gq.so"
 SOURCES = ["fp8gq_api.cu"]
-HEADERS = ["fp8gq_device.cuh", "gemv_row.cuh", "gemm_tm.cuh", "quant_only.cuh"]
+HEADERS = ["fp8gq_device.cuh", "gemv_row.cuh", "gemm_tm.cuh", "quant_only.cuh", "swiglu_writer.cuh",
+           "add_rmsnorm.cuh", "stack.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -44,6 +44,25 @@ class Gather(ctypes.Structure):
                 ("local_out", ctypes.c_int)]
 
 
+class StackLinear(ctypes.Structure):
+    """struct fp8gq_stack_linear (include/fp8gq.h)."""
+    _fields_ = [("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
+                ("w", ctypes.c_void_p), ("ldw", ctypes.c_int64),
+                ("ws", ctypes.c_void_p), ("ldws", ctypes.c_int64),
+                ("out", ctypes.c_void_p), ("ldo", ctypes.c_int64),
+                ("N", ctypes.c_int), ("K", ctypes.c_int),
+                ("swiglu", ctypes.c_int), ("reserved", ctypes.c_int)]
+
+
+class StackPlan(ctypes.Structure):
+    """struct fp8gq_stack_plan (include/fp8gq.h)."""
+    _fields_ = [("device", ctypes.c_void_p), ("bytes", ctypes.c_size_t),
+                ("n", ctypes.c_int), ("M", ctypes.c_int), ("device_id", ctypes.c_int), ("grid", ctypes.c_int),
+                ("stages", ctypes.c_int), ("npw", ctypes.c_int),
+                ("sw", ctypes.c_int), ("lg_sw", ctypes.c_int), ("kpb", ctypes.c_int), ("nacc", ctypes.c_int),
+                ("smem", ctypes.c_size_t), ("reserved", ctypes.c_int64 * 4)]
+
+
 # name -> (restype, argtypes); the order of include/fp8gq.h
 _P = ctypes.c_void_p
 _I = ctypes.c_int
@@ -78,6 +97,10 @@ SIGNATURES = {
     "fp8gq_swiglu_quant": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I, _I, _P]),
     "fp8gq_set_static_weights": (_I, [_I]),
     "fp8gq_set_tm_options": (_I, [_I]),
+    "fp8gq_stack_plan_bytes": (_SZ, [_I, _I]),
+    "fp8gq_stack_dependencies": (_I, [ctypes.POINTER(StackLinear), _I, _I, ctypes.POINTER(_I)]),
+    "fp8gq_stack_prepare": (_I, [ctypes.POINTER(StackLinear), _I, _I, _P, _SZ, ctypes.POINTER(StackPlan), _P]),
+    "fp8gq_stack_run": (_I, [ctypes.POINTER(StackPlan), _P]),
     "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),
 }
 
