@@ -23,7 +23,7 @@
 // cooperative grid, so every CTA is resident and every wait ends.
 //
 // Work split (per linear, stream-K): the N/128 x K/128 tiles, row-block
-// major; CTA i takes tiles [i*U/G, (i+1)*U/G).  A row block split between
+// major, over Gl = min(G, U) CTAs; CTA i < Gl takes tiles [i*U/Gl, (i+1)*U/Gl).  A row block split between
 // CTAs leaves fp32 partial sums in the plan's scratch, and the CTA that
 // finishes it last adds them in CTA order (tile-kernel protocol).  Partial
 // slots and split counters alternate between two banks by linear parity; a
@@ -143,9 +143,12 @@ __device__ __forceinline__ void st_acquire_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// CTA i's range of linear l: J tiles from row block nb0, K block kb0.
+// CTA i's range of linear l: J tiles from row block nb0, K block kb0.  A
+// linear with U tiles is spread over Gl = min(G, U) CTAs, so that every CTA
+// below Gl holds at least one tile (the split-K hand-off counts on it); CTAs
+// from Gl on have none.
 struct StRange {
-  int64_t u0, U;
+  int64_t u0, U, Gl;
   int J, nb0, kb0, KB;
 };
 
@@ -153,8 +156,10 @@ __device__ __forceinline__ StRange st_range(const StackLinear* L, int64_t G, int
   StRange r;
   r.U = __ldg(&L->U);
   r.KB = __ldg(&L->KB);
-  r.u0 = (i * r.U) / G;
-  const int64_t u1 = ((i + 1) * r.U) / G;
+  r.Gl = r.U < G ? r.U : G;
+  const int64_t ic = i < r.Gl ? i : r.Gl;
+  r.u0 = (ic * r.U) / r.Gl;
+  const int64_t u1 = i < r.Gl ? ((i + 1) * r.U) / r.Gl : r.u0;
   r.J = static_cast<int>(u1 - r.u0);
   r.nb0 = static_cast<int>(r.u0 / r.KB);
   r.kb0 = static_cast<int>(r.u0 - static_cast<int64_t>(r.nb0) * r.KB);
@@ -532,8 +537,8 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
             named_bar_sync(2, 128);
             const int64_t first_u = static_cast<int64_t>(nb) * r.KB;
             const int64_t last_u = first_u + r.KB - 1;
-            const int64_t i_lo = ((first_u + 1) * G - 1) / r.U;
-            const int64_t i_hi = ((last_u + 1) * G - 1) / r.U;
+            const int64_t i_lo = ((first_u + 1) * r.Gl - 1) / r.U;   // owners of its first and last tile
+            const int64_t i_hi = ((last_u + 1) * r.Gl - 1) / r.U;
             int* counter = p.counters + bank * kStMaxRowBlocks + nb;
             if (tid == 192) {
               const int old = atomic_add_acq_rel_gpu(counter, 1);
@@ -547,7 +552,7 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
 #pragma unroll
               for (int m = 0; m < kStMT; ++m) sum[m] = 0.0f;
               for (int64_t i = i_lo; i <= i_hi; ++i) {
-                const int64_t ui0 = (i * r.U) / G;
+                const int64_t ui0 = (i * r.U) / r.Gl;
                 const int si = (ui0 / r.KB == nb) ? 0 : 1;
                 const float* pi = p.partials + (((static_cast<int64_t>(bank) * G + i) * 2 + si) * M) * 128;
 #pragma unroll
