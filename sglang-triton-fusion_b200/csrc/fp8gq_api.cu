@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <utility>
@@ -74,6 +76,14 @@ int check_common(const void* x, const void* w, const float* ws, const void* out,
   if ((reinterpret_cast<uintptr_t>(ws) & 3u) != 0 || (reinterpret_cast<uintptr_t>(out) & 1u) != 0)
     return FP8GQ_ERR_ALIGNMENT;
   return FP8GQ_OK;
+}
+
+// FP8GQ_ERR_LAUNCH for a failed CUDA call; with FP8GQ_DEBUG set in the
+// environment the CUDA error is also printed to stderr.
+int cuda_fail(cudaError_t e, const char* what) {
+  static const bool debug = std::getenv("FP8GQ_DEBUG") != nullptr;
+  if (debug) std::fprintf(stderr, "fp8gq: %s: %s\n", what, cudaGetErrorString(e));
+  return FP8GQ_ERR_LAUNCH;
 }
 
 inline int launch_status() {
@@ -676,10 +686,13 @@ int fp8gq_stack_prepare(const fp8gq_stack_linear* lin, int n, int M, void* devic
   const int G = di.sm_count;
   if (bytes < st_plan_bytes(n, M, G) || (reinterpret_cast<uintptr_t>(device_mem) & 255u))
     return FP8GQ_ERR_WORKSPACE;
-  // ring depth from the shared memory one CTA per SM may use
-  const int64_t avail = static_cast<int64_t>(di.max_smem_optin) - static_cast<int64_t>(kStTailBytes) - 1024;
+  // ring depth from the shared memory one CTA per SM may use (the resident
+  // activation region takes what the ring leaves)
+  const int64_t avail = static_cast<int64_t>(di.max_smem_optin) - static_cast<int64_t>(kStTailBytes) - 1024 -
+                        kStWsLin * 4 - 64 * 132;
   const int S = st_pick_stages(avail / (kTmATileBytes + kStBTileBytes));
-  if (S < 4) return FP8GQ_ERR_UNSUPPORTED;
+  StLayout lo;
+  if (S < 4 || !st_layout(S, di.max_smem_optin, &lo)) return FP8GQ_ERR_UNSUPPORTED;
   std::vector<int> dep(n);
   stack_deps(lin, n, M, dep.data());
   std::vector<StackLinear> table(n);
@@ -727,7 +740,7 @@ int fp8gq_stack_prepare(const fp8gq_stack_linear* lin, int n, int M, void* devic
   plan->lg_sw = lg;
   plan->kpb = kStMT / sw;
   plan->nacc = plan->kpb >= 8 ? 2 : kTmMaxAcc;
-  plan->smem = static_cast<size_t>(S) * (kTmATileBytes + kStBTileBytes) + kStTailBytes + 1024;
+  plan->smem = lo.smem;
   return FP8GQ_OK;
 }
 
@@ -757,18 +770,34 @@ int fp8gq_stack_run(const fp8gq_stack_plan* plan, fp8gq_stream_t stream) {
   p.nacc = plan->nacc;
   p.stages = plan->stages;
   p.npw = plan->npw;
-  p.b_off = static_cast<uint32_t>(plan->stages * kTmATileBytes);
-  p.bar_off = p.b_off + static_cast<uint32_t>(plan->stages * kStBTileBytes);
-  if (cudaFuncSetAttribute(stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(plan->smem)) != cudaSuccess)
-    return FP8GQ_ERR_LAUNCH;
+  StLayout lo;
+  if (!st_layout(plan->stages, di.max_smem_optin, &lo) || lo.smem != plan->smem) return FP8GQ_ERR_UNSUPPORTED;
+  p.b_off = lo.b_off;
+  p.bar_off = lo.bar_off;
+  p.res_off = lo.res_off;
+  p.res_groups = lo.res_groups;
+  cudaError_t e = cudaFuncSetAttribute(stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(plan->smem));
+  if (e != cudaSuccess) return cuda_fail(e, "stack_kernel shared memory attribute");
   // every CTA must be resident at once (they wait for one another): one CTA
   // per SM, launched as a cooperative grid, which the runtime refuses rather
   // than run partly
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel, kStThreads, plan->smem) != cudaSuccess ||
-      per_sm < 1)
-    return FP8GQ_ERR_UNSUPPORTED;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, stack_kernel, kStThreads, plan->smem);
+  if (e != cudaSuccess) return cuda_fail(e, "stack_kernel occupancy");
+  if (per_sm < 1) {
+    if (std::getenv("FP8GQ_DEBUG")) {
+      cudaFuncAttributes fa;
+      int per_sm0 = -1;
+      cudaFuncGetAttributes(&fa, stack_kernel);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm0, stack_kernel, kStThreads, 0);
+      std::fprintf(stderr, "fp8gq: stack_kernel regs %d, max threads %d, static smem %zu, local %zu, "
+                   "max dynamic smem %d; CTAs per SM with %zu B: 0, with 0 B: %d\n", fa.numRegs,
+                   fa.maxThreadsPerBlock, fa.sharedSizeBytes, fa.localSizeBytes, fa.maxDynamicSharedSizeBytes,
+                   plan->smem, per_sm0);
+    }
+    return cuda_fail(cudaErrorInvalidConfiguration, "stack_kernel: no CTA fits on an SM");
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan->grid);
   cfg.blockDim = dim3(kStThreads);
@@ -779,8 +808,10 @@ int fp8gq_stack_run(const fp8gq_stack_plan* plan, fp8gq_stream_t stream) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, stack_kernel, p) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
-  return launch_status();
+  e = cudaLaunchKernelEx(&cfg, stack_kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "stack_kernel launch");
+  e = cudaGetLastError();
+  return e == cudaSuccess ? FP8GQ_OK : cuda_fail(e, "stack_kernel launch");
 }
 
 }  // extern "C"

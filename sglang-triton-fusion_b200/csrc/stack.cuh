@@ -57,6 +57,7 @@ constexpr int kStMaxLinears = 4096;
 constexpr int kStMaxRowBlocks = 4096;     // N <= 524288
 constexpr int kStBTileBytes = kStMT * 128;
 constexpr int kStTmemCols = 64;           // 4 accumulator buffers of 16 columns
+constexpr int kStWsLin = 1024;            // block scales of a CTA's tiles of one linear kept in shared memory
 
 // One linear of the list, as the kernel reads it (device memory, 256 bytes).
 struct alignas(64) StackLinear {
@@ -79,7 +80,8 @@ struct StackParams {
   int* counters;            // [2][kStMaxRowBlocks] split-K counters, zero on entry and exit
   float* partials;          // [2][G][2][M][128]
   int n, M, sw, lg_sw, kpb, nacc, stages, npw;
-  uint32_t b_off, bar_off;
+  uint32_t b_off, bar_off, res_off;
+  int res_groups;           // (token, K block) groups the resident region holds
 };
 
 // Shared memory from the 1 KB-aligned base: A tiles [S][16 KB] | B tiles
@@ -213,6 +215,11 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
   volatile uint32_t* sx_tag = misc + 4;                               // [kStRing]
   float* ws_ring = reinterpret_cast<float*>(misc + 4 + kStRing);      // [kStRing]
   float* sx_ring = ws_ring + kStRing;                                 // [kStRing][16]
+  // per-linear activation region: res_xq [res_groups][128 B], sx_res
+  // [res_groups], ws_lin [kStWsLin]
+  uint8_t* res_xq = smem + p.res_off;
+  float* sx_res = reinterpret_cast<float*>(res_xq + static_cast<size_t>(p.res_groups) * 128);
+  float* ws_lin = sx_res + p.res_groups;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -312,22 +319,29 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
     }
   } else if (warp < 6) {
     // ----------------------------------------- activation producers --
-    // Warp w takes the tiles t (numbered over the whole list) with
-    // t % npw == w - 2; npw divides S, so a stage is always this warp's.
-    // Lane l covers the 16-byte chunk l % 8 of B-tile rows l / 8 + 4 i.
+    // Per linear, all four warps together: the block scales of the CTA's
+    // tiles into ws_lin, the dependency wait, then (resident feed) the
+    // activation of the CTA's K blocks quantised once into res_xq / sx_res.
+    // Then warp w copies the B tiles of the tiles t (numbered over the whole
+    // list) with t % npw == w - 2 (npw divides S, so a stage is always the
+    // same warp's) from the resident bytes, or -- where M x (K blocks) does
+    // not fit -- quantises each K block from global memory itself.  The four
+    // warps meet at named barrier 4 at every linear, on every path.
     const int NPW = p.npw;
     const int w4 = warp - 2;
+    const int aw = tid - 64;                  // 0 .. 127
     const int chunk = lane & 7;
     const int row0 = lane >> 3;
+    const int oct = w4 * 4 + (lane >> 3);     // lane octet among the four warps, 0 .. 15
     const int M = p.M;
     const int sw = p.sw;
-    bool ok = w4 < NPW;
+    bool ok = true;
     int64_t t = 0;            // tile number over the list
     StRing rg;
-    for (int l = 0; l < p.n && ok; ++l) {
+    for (int l = 0; l < p.n; ++l) {
       const StackLinear* L = p.lin + l;
       const StRange r = st_range(L, G, cta);
-      if (r.J == 0) continue;
+      if (r.J == 0) continue;                 // the same for the four warps
       const int dep = __ldg(&L->dep);
       const int swiglu = __ldg(&L->swiglu);
       const __nv_bfloat16* x = L->x;
@@ -335,62 +349,59 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
       const float* ws = L->ws;
       const int64_t ldws = __ldg(&L->ldws);
       const int K = __ldg(&L->K);
-      bool dep_done = dep < 0;
-      StCursor c;
-      c.init(r);
-      for (int j = 0; j < r.J; ++j, c.next(r.KB, kpb), rg.next(S), ++t) {
-        if (static_cast<int>(t % NPW) != w4) continue;
-        // the block scale first: it does not depend on the activation
-        const float wsv = __ldg(ws + static_cast<int64_t>(c.nb) * ldws + c.kb);
-        if (!dep_done) {
-          uint32_t okd = 1;
-          if (lane == 0) okd = st_wait_count(p.done + dep, static_cast<unsigned int>(G)) ? 1u : 0u;
-          __syncwarp();
-          okd = __shfl_sync(0xffffffffu, okd, 0);
-          if (!okd) {
-            ok = false;
-            break;
-          }
-          dep_done = true;
+      const bool res_full = r.J >= r.KB;      // resident slot = K block; else slot = tile j
+      const int nkb = res_full ? r.KB : r.J;
+      const bool resident = M * nkb <= p.res_groups;
+      const bool ws_pre = r.J <= kStWsLin;
+      // the previous linear's copies (readers of res_xq, sx_res, ws_lin) are done
+      named_bar_sync(4, 128);
+      if (ws_pre) {
+        for (int j = aw; j < r.J; j += 128) {
+          const int tk = r.kb0 + j;
+          const int dn = tk / r.KB;
+          ws_lin[j] = __ldg(ws + static_cast<int64_t>(r.nb0 + dn) * ldws + (tk - dn * r.KB));
         }
-        // this lane's rows of the B tile: row br holds token m = br - pos*sw
-        uint4 wd[4][4];
+      }
+      if (dep >= 0) {
+        uint32_t okd = ok ? 1u : 0u;
+        if (ok && lane == 0) okd = st_wait_count(p.done + dep, static_cast<unsigned int>(G)) ? 1u : 0u;
+        __syncwarp();
+        ok = __shfl_sync(0xffffffffu, okd, 0) != 0;
+      }
+      if (resident) {
+        // group g: token m = g / nkb, slot q = g % nkb; the loads of kPasses
+        // passes are issued before any of them is quantised (one L2 round
+        // trip for up to 64 groups)
+        constexpr int kPasses = 4;
+        const int ngroups = M * nkb;
+        for (int g0 = 0; g0 < ngroups; g0 += 16 * kPasses) {
+          uint4 wd[kPasses][4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int br = row0 + 4 * i;
-          const int m = br - c.pos * sw;
-          const bool live = m >= 0 && m < sw && m < M;
-          if (live) {
-            const uint4* xr =
-                reinterpret_cast<const uint4*>(x + static_cast<int64_t>(m) * ldx + c.kb * 128 + chunk * 16);
-            wd[i][0] = __ldcg(xr);
-            wd[i][1] = __ldcg(xr + 1);
-            if (swiglu) {
-              const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(xr) + K);
-              wd[i][2] = __ldcg(ur);
-              wd[i][3] = __ldcg(ur + 1);
+          for (int i = 0; i < kPasses; ++i) {
+            const int g = g0 + 16 * i + oct;
+            if (ok && g < ngroups) {
+              const int m = g / nkb;
+              const int q = g - m * nkb;
+              int kb = res_full ? q : r.kb0 + q;
+              if (kb >= r.KB) kb -= r.KB;
+              const uint4* xr =
+                  reinterpret_cast<const uint4*>(x + static_cast<int64_t>(m) * ldx + kb * 128 + chunk * 16);
+              wd[i][0] = __ldcg(xr);
+              wd[i][1] = __ldcg(xr + 1);
+              if (swiglu) {
+                const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(xr) + K);
+                wd[i][2] = __ldcg(ur);
+                wd[i][3] = __ldcg(ur + 1);
+              }
             }
           }
-        }
-        if (t >= S) {
-          uint32_t oke = 1;
-          if (lane == 0) oke = st_mbar_wait(&empty[rg.s], rg.ph ^ 1u, kSiteStackRing) ? 1u : 0u;
-          __syncwarp();
-          oke = __shfl_sync(0xffffffffu, oke, 0);
-          if (!oke) {
-            ok = false;
-            break;
-          }
-        }
-        uint8_t* btile = b_tiles + rg.s * kStBTileBytes;
-        float* sxs = sx_ring + (t & (kStRing - 1)) * kStMT;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int br = row0 + 4 * i;
-          const int m = br - c.pos * sw;
-          const bool live = m >= 0 && m < sw && m < M;
-          uint4 packed = make_uint4(0u, 0u, 0u, 0u);
-          if (__any_sync(0xffffffffu, live)) {    // rows of a lane octet are all live or all not
+          for (int i = 0; i < kPasses; ++i) {
+            if (g0 + 16 * i >= ngroups) continue;   // the same for every lane
+            const int g = g0 + 16 * i + oct;
+            const bool live = ok && g < ngroups;  // the same within a lane octet
+            const int m = live ? g / nkb : 0;
+            const int q = live ? g - m * nkb : 0;
             float v[16];
             if (live) {
               if (swiglu)
@@ -402,10 +413,81 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
               for (int e = 0; e < 16; ++e) v[e] = 0.0f;
             }
             float sx;
-            packed = quant16_octet(v, live, sx);
-            if (live && chunk == 0) sxs[m] = sx;
+            const uint4 packed = quant16_octet(v, live, sx);
+            if (live) {
+              *reinterpret_cast<uint4*>(res_xq + (static_cast<int64_t>(q) * M + m) * 128 + chunk * 16) = packed;
+              if (chunk == 0) sx_res[q * M + m] = sx;
+            }
           }
-          *reinterpret_cast<uint4*>(btile + br * 128 + ((chunk ^ (br & 7)) << 4)) = packed;
+        }
+      }
+      if (resident || ws_pre) named_bar_sync(4, 128);   // resident bytes, scales and ws_lin written
+      StCursor c;
+      c.init(r);
+      for (int j = 0; j < r.J; ++j, c.next(r.KB, kpb), rg.next(S), ++t) {
+        if (static_cast<int>(t % NPW) != w4 || !ok) continue;
+        const float wsv = ws_pre ? ws_lin[j] : __ldg(ws + static_cast<int64_t>(c.nb) * ldws + c.kb);
+        uint8_t* btile = b_tiles + rg.s * kStBTileBytes;
+        float* sxs = sx_ring + (t & (kStRing - 1)) * kStMT;
+        if (resident) {
+          if (t >= S) {
+            uint32_t oke = 1;
+            if (lane == 0) oke = st_mbar_wait(&empty[rg.s], rg.ph ^ 1u, kSiteStackRing) ? 1u : 0u;
+            __syncwarp();
+            ok = __shfl_sync(0xffffffffu, oke, 0) != 0;
+            if (!ok) continue;
+          }
+          const int q = res_full ? c.kb : j;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int br = row0 + 4 * i;
+            const int m = br - c.pos * sw;
+            const bool live = m >= 0 && m < sw && m < M;
+            uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+            if (live) {
+              packed = *reinterpret_cast<const uint4*>(res_xq + (static_cast<int64_t>(q) * M + m) * 128 + chunk * 16);
+              if (chunk == 0) sxs[m] = sx_res[q * M + m];
+            }
+            *reinterpret_cast<uint4*>(btile + br * 128 + ((chunk ^ (br & 7)) << 4)) = packed;
+          }
+        } else {
+          // M x (K blocks) does not fit the resident region: quantise this
+          // K block from global memory, one row of the lane's four at a time
+          if (t >= S) {
+            uint32_t oke = 1;
+            if (lane == 0) oke = st_mbar_wait(&empty[rg.s], rg.ph ^ 1u, kSiteStackRing) ? 1u : 0u;
+            __syncwarp();
+            ok = __shfl_sync(0xffffffffu, oke, 0) != 0;
+            if (!ok) continue;
+          }
+#pragma unroll 1
+          for (int i = 0; i < 4; ++i) {
+            const int br = row0 + 4 * i;             // row br of the B tile holds token br - pos*sw
+            const int m = br - c.pos * sw;
+            const bool live = m >= 0 && m < sw && m < M;
+            uint4 packed = make_uint4(0u, 0u, 0u, 0u);
+            if (__any_sync(0xffffffffu, live)) {    // rows of a lane octet are all live or all not
+              float v[16];
+              if (live) {
+                const uint4* xr =
+                    reinterpret_cast<const uint4*>(x + static_cast<int64_t>(m) * ldx + c.kb * 128 + chunk * 16);
+                const uint4 xa = __ldcg(xr), xb = __ldcg(xr + 1);
+                if (swiglu) {
+                  const uint4* ur = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(xr) + K);
+                  act16<true>(v, xa, xb, __ldcg(ur), __ldcg(ur + 1));
+                } else {
+                  act16<false>(v, xa, xb, xa, xb);
+                }
+              } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+              }
+              float sx;
+              packed = quant16_octet(v, live, sx);
+              if (live && chunk == 0) sxs[m] = sx;
+            }
+            *reinterpret_cast<uint4*>(btile + br * 128 + ((chunk ^ (br & 7)) << 4)) = packed;
+          }
         }
         if (lane == 0) ws_ring[t & (kStRing - 1)] = wsv;
         fence_proxy_async_smem();
@@ -605,8 +687,29 @@ inline size_t st_plan_bytes(int n, int M, int G) {
   return st_table_bytes(n) + st_done_bytes(n) + st_counter_bytes() + st_partial_bytes(M, G);
 }
 
-// Ring depth from the shared memory: 12, 8, 6 or 4 stages (the activation
-// warps in use divide the depth).
-inline int st_pick_stages(int64_t fit) { return fit >= 12 ? 12 : fit >= 8 ? 8 : fit >= 6 ? 6 : fit >= 4 ? 4 : 0; }
+// Ring depth: 8 stages (or 6 or 4 where shared memory is short; the
+// activation warps in use divide the depth), leaving the rest of the shared
+// memory to the per-linear resident activation.
+inline int st_pick_stages(int64_t fit) { return fit >= 8 ? 8 : fit >= 6 ? 6 : fit >= 4 ? 4 : 0; }
+
+// Shared-memory layout of a launch with S stages: the ring, the barrier and
+// ring tail, then the resident activation region with what is left.
+struct StLayout {
+  uint32_t b_off, bar_off, res_off;
+  int res_groups;
+  size_t smem;
+};
+inline bool st_layout(int S, int max_smem, StLayout* lo) {
+  lo->b_off = static_cast<uint32_t>(S * kTmATileBytes);
+  lo->bar_off = lo->b_off + static_cast<uint32_t>(S * kStBTileBytes);
+  lo->res_off = lo->bar_off + static_cast<uint32_t>((kStTailBytes + 15) / 16 * 16);
+  // 4 KB below the per-block limit: headroom for the runtime's own
+  // per-block shared memory, so that one CTA per SM always fits
+  const int64_t left = static_cast<int64_t>(max_smem) - 4096 - 1024 - lo->res_off - kStWsLin * 4;
+  if (left < 0) return false;
+  lo->res_groups = static_cast<int>(left / (128 + 4));
+  lo->smem = 1024 + lo->res_off + static_cast<size_t>(lo->res_groups) * (128 + 4) + kStWsLin * 4;
+  return lo->smem <= static_cast<size_t>(max_smem);
+}
 
 }  // namespace fp8gq
