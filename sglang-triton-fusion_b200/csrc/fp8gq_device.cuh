@@ -189,11 +189,12 @@ __device__ __forceinline__ float exp_cw(float x) {
   const float kLog2e = 1.44269504088896341f;
   const float kC1 = 0.693359375f;
   const float kC2 = -2.12194440e-4f;
-  if (x != x) return x;
-  if (x > 88.0f) return __int_as_float(0x7f800000);
-  if (x < -88.0f) return 0.0f;
-  const float n = rintf(__fmul_rn(x, kLog2e));
-  float r = __fsub_rn(x, __fmul_rn(n, kC1));
+  // Branch-free: the polynomial runs on x clamped to [-88, 88] (inputs in
+  // range are unchanged), and the out-of-range and NaN results are selected
+  // at the end, so that the unrolled evaluations of a lane interleave.
+  const float xc = fminf(fmaxf(x, -88.0f), 88.0f);
+  const float n = rintf(__fmul_rn(xc, kLog2e));
+  float r = __fsub_rn(xc, __fmul_rn(n, kC1));
   r = __fsub_rn(r, __fmul_rn(n, kC2));
   float p = 1.9875691500e-4f;
   p = __fadd_rn(__fmul_rn(p, r), 1.3981999507e-3f);
@@ -205,11 +206,14 @@ __device__ __forceinline__ float exp_cw(float x) {
   p = __fadd_rn(p, r);
   p = __fadd_rn(p, 1.0f);
   const int ni = static_cast<int>(n);
-  const int h1 = (ni >= 0) ? (ni / 2) : -((-ni + 1) / 2);  // floor(n / 2)
+  const int h1 = ni >> 1;                  // floor(n / 2)
   const int h2 = ni - h1;
   const float s1 = __int_as_float((h1 + 127) << 23);
   const float s2 = __int_as_float((h2 + 127) << 23);
-  return __fmul_rn(__fmul_rn(p, s1), s2);
+  float out = __fmul_rn(__fmul_rn(p, s1), s2);
+  out = x > 88.0f ? __int_as_float(0x7f800000) : out;
+  out = x < -88.0f ? 0.0f : out;
+  return x != x ? x : out;
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) {

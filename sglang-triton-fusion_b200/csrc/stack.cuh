@@ -519,6 +519,15 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
       __nv_bfloat16* out = L->out;
       const int64_t ldo = __ldg(&L->ldo);
       int seg_j0 = 0, seg_kb0 = 0;
+      // The partial bank of linear l was last used by linear l - 2: before
+      // any partial of l is written every CTA must be past l - 2.  Checked
+      // here, at the start of the linear, off the path of its last group.
+      if (l >= 2 && r.J > 0) {
+        uint32_t okw = ok ? 1u : 0u;
+        if (ok && lane == 0) okw = st_wait_count(p.done + (l - 2), static_cast<unsigned int>(G)) ? 1u : 0u;
+        __syncwarp();
+        ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+      }
       StCursor c;
       c.init(r);
       for (int j = 0; j < r.J; ++j, c.next(r.KB, kpb), ++t) {
@@ -599,15 +608,8 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
             for (int m = 0; m < kStMT; ++m)
               if (m < M) out[static_cast<int64_t>(m) * ldo + n] = __float2bfloat16_rn(acc[m]);
           } else {
-            // partial row block: publish, count, and let the last CTA reduce.
-            // The bank of linear l was last used by linear l - 2: wait until
-            // every CTA is past it.
-            if (l >= 2) {
-              uint32_t okw = ok ? 1u : 0u;
-              if (ok && lane == 0) okw = st_wait_count(p.done + (l - 2), static_cast<unsigned int>(G)) ? 1u : 0u;
-              __syncwarp();
-              ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
-            }
+            // partial row block: publish, count, and let the last CTA reduce
+            // (the bank is free: see the wait at the start of the linear)
             const int slot = (seg_j0 == 0) ? 0 : 1;
             float* mine = p.partials + (((static_cast<int64_t>(bank) * G + cta) * 2 + slot) * M) * 128;
 #pragma unroll
