@@ -149,9 +149,7 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   if (smem > static_cast<size_t>(di.max_smem_optin)) return FP8GQ_ERR_UNSUPPORTED;
 
   RowKernel fn = swiglu ? row_lookup<true>(ci, ri) : row_lookup<false>(ci, ri);
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-      cudaSuccess)
-    return FP8GQ_ERR_LAUNCH;
+  if (ensure_max_smem(reinterpret_cast<const void*>(fn), di.max_smem_optin) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
 
   RowParams p;
   p.x = static_cast<const __nv_bfloat16*>(x);

@@ -1220,6 +1220,70 @@ inline bool make_act_tmap(CUtensorMap* map, const void* x, int rows, int64_t col
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Host-side caches for the per-call set-up of a launch.  A tensor map
+// depends only on the address, the shape, the row stride and the box, so an
+// encoded one is reused for the same operand (a decode loop calls every
+// linear on the same weights and activation buffers); the table is cleared
+// when it grows past kTmapCacheMax entries.
+struct TmapKey {
+  int dev, kind, rows, box_rows;
+  const void* ptr;
+  int64_t cols, ld;
+  bool operator<(const TmapKey& o) const {
+    return std::tie(dev, kind, rows, box_rows, ptr, cols, ld) <
+           std::tie(o.dev, o.kind, o.rows, o.box_rows, o.ptr, o.cols, o.ld);
+  }
+};
+constexpr size_t kTmapCacheMax = 8192;
+
+// kind 0: weight (make_weight_tmap), 1: bf16 activation (make_act_tmap),
+// 2: pre-quantised activation (make_xq_tmap, box_rows = MT)
+inline bool cached_tmap(CUtensorMap* map, int kind, const void* ptr, int rows, int64_t cols, int64_t ld,
+                        int box_rows) {
+  static std::mutex mu;
+  static std::map<TmapKey, CUtensorMap> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const TmapKey key{dev, kind, rows, box_rows, ptr, cols, ld};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+      *map = it->second;
+      return true;
+    }
+  }
+  bool ok = kind == 0   ? make_weight_tmap(map, ptr, rows, static_cast<int>(cols), ld)
+            : kind == 1 ? make_act_tmap(map, ptr, rows, cols, ld)
+                        : make_xq_tmap(map, ptr, rows, static_cast<int>(cols), box_rows);
+  if (!ok) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() >= kTmapCacheMax) cache.clear();
+  cache.emplace(key, *map);
+  return true;
+}
+
+// cudaFuncAttributeMaxDynamicSharedMemorySize raised to the device's limit
+// once per kernel and device (launches then pass their own smaller sizes).
+inline cudaError_t ensure_max_smem(const void* fn, int max_smem) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_pair(dev, fn);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= max_smem) return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  done[key] = max_smem;
+  return cudaSuccess;
+}
+
 // Shared-memory plan of one pass: ring depth, activation mode and layout.
 struct TmPlan {
   int stages, npw, resident;
@@ -1286,8 +1350,7 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
     return 8;  // FP8GQ_ERR_UNSUPPORTED
   if (p.norm.norm && !pl.resident) return 8;
   auto fn = gemm_tm_kernel<MT, SW>;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) != cudaSuccess)
-    return 7;  // FP8GQ_ERR_LAUNCH
+  if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) != cudaSuccess) return 7;  // FP8GQ_ERR_LAUNCH
   p.stages = pl.stages;
   p.npw = pl.npw;
   p.resident = pl.resident;
@@ -1314,7 +1377,7 @@ int tm_max_clusters(int csize, size_t smem, int max_smem) {
   if (it != cache.end()) return it->second;
   auto fn = gemm_tm_kernel<MT, SW>;
   int n = 0;
-  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem) == cudaSuccess) {
+  if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(csize);
     cfg.blockDim = dim3(kTmThreads);
@@ -1398,7 +1461,7 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return 5;  // FP8GQ_ERR_WORKSPACE
   CUtensorMap tmap_w;
-  if (!make_weight_tmap(&tmap_w, w, N, K, ldw)) return 7;
+  if (!cached_tmap(&tmap_w, 0, w, N, K, ldw, 0)) return 7;
   TmParams p;
   p.ws = ws;
   p.ldws = ldws;
@@ -1515,8 +1578,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     p.sx_pre = pre ? pre_sx + static_cast<int64_t>(m0) * p.KB : nullptr;
     CUtensorMap tmap_x;
     if (pre) {
-      if (!make_xq_tmap(&tmap_x, pre_xq + static_cast<int64_t>(m0) * K, p.M, K, MT)) return 7;
-    } else if (!make_act_tmap(&tmap_x, xp, p.M, xcols, ldx)) {
+      if (!cached_tmap(&tmap_x, 2, pre_xq + static_cast<int64_t>(m0) * K, p.M, K, K, MT)) return 7;
+    } else if (!cached_tmap(&tmap_x, 1, xp, p.M, xcols, ldx, 0)) {
       return 7;
     }
     int st;

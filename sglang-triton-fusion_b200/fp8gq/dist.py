@@ -178,7 +178,7 @@ class PeerGather:
         if out.shape != (M, Nr * self.world):
             raise ops.ShapeError(f"out must be [{M}, {Nr * self.world}], got {tuple(out.shape)}")
         g = desc if desc is not None else self.descriptor(out, self.rank * Nr, wait_input)
-        nbytes = self.lib.fp8gq_workspace_bytes(M, Nr, K)
+        nbytes = ops._workspace_bytes(self.lib, x.device, M, Nr, K)
         ws_buf = ops.workspace(x.device, nbytes) if nbytes else None
         st = self.lib.fp8gq_fused_gemv_quant_gather(
             x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), Wq_shard.stride(0), Ws_shard.data_ptr(),
@@ -229,7 +229,7 @@ class PeerGather:
             raise ops.ShapeError(f"x must be [M, {Kr}], got {tuple(x.shape)}")
         ops._check_weight(Wq_cols, Ws_cols, Kr)
         g = desc if desc is not None else self.partial_descriptor(slabs)
-        nbytes = self.lib.fp8gq_workspace_bytes(M, N, Kr)
+        nbytes = ops._workspace_bytes(self.lib, x.device, M, N, Kr)
         ws_buf = ops.workspace(x.device, nbytes) if nbytes else None
         fn = self.lib.fp8gq_fused_swiglu_q_gemm_gather if swiglu else self.lib.fp8gq_fused_gemv_quant_gather
         st = fn(x.data_ptr(), x.stride(0), Wq_cols.data_ptr(), Wq_cols.stride(0), Ws_cols.data_ptr(),

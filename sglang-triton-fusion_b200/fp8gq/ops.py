@@ -23,18 +23,38 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
+try:
+    _raw_stream = torch._C._cuda_getCurrentRawStream   # the current stream's handle, without a Stream object
+except AttributeError:                                  # pragma: no cover
+    _raw_stream = None
+
+
 def _stream(device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
 _workspaces: dict = {}
+_ws_bytes: dict = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def _workspace_bytes(lib, device, M, N, K, tile_only=False) -> int:
+    """fp8gq_workspace_bytes, remembered per (device, shape)."""
+    key = (device.index, M, N, K, tile_only)
+    n = _ws_bytes.get(key)
+    if n is None:
+        n = lib.fp8gq_workspace_bytes(max(M, 2) if tile_only else M, N, K)
+        _ws_bytes[key] = n
+    return n
+
+
+def workspace(device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
     """Zero-filled scratch kept per (device, stream).  The kernels leave it
     zero-filled when they finish, so it is allocated and cleared once; grow it
     (and warm every shape up) before capturing a CUDA graph."""
-    stream = _stream(device)
+    if stream is None:
+        stream = _stream(device)
     key = (device.index, stream)
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
@@ -101,8 +121,8 @@ def fused_gemv_quant(x: torch.Tensor, Wq: torch.Tensor, Ws: torch.Tensor, *, out
                                       N, K, _ptr(xq), _ptr(sx), stream)
         _lib.check(st, "fp8gq_gemv_quant_row")
     else:
-        nbytes = lib.fp8gq_workspace_bytes(M, N, K) if kernel == "auto" else _tm_ws_bytes(lib, M, N, K)
-        ws_buf = workspace(x.device, nbytes) if nbytes else None
+        nbytes = _workspace_bytes(lib, x.device, M, N, K, tile_only=kernel != "auto")
+        ws_buf = workspace(x.device, nbytes, stream) if nbytes else None
         fn = lib.fp8gq_fused_gemv_quant if kernel == "auto" else lib.fp8gq_gemv_quant_tm
         if kernel not in ("auto", "tm"):
             raise ValueError(f"unknown kernel {kernel!r}")
@@ -110,11 +130,6 @@ def fused_gemv_quant(x: torch.Tensor, Wq: torch.Tensor, Ws: torch.Tensor, *, out
                 M, N, K, _ptr(xq), _ptr(sx), _ptr(ws_buf), 0 if ws_buf is None else ws_buf.numel(), stream)
         _lib.check(st, fn.__name__)
     return (out, xq, sx) if return_quant else out
-
-
-def _tm_ws_bytes(lib, M, N, K):
-    # the tile kernel's scratch, also for M == 1 (which "auto" sends to the row kernel)
-    return lib.fp8gq_workspace_bytes(max(M, 2), N, K)
 
 
 def fused_swiglu_q_gemm(gu: torch.Tensor, Wd: torch.Tensor, Ws: torch.Tensor, *, out=None,
@@ -136,7 +151,7 @@ def fused_swiglu_q_gemm(gu: torch.Tensor, Wd: torch.Tensor, Ws: torch.Tensor, *,
         out = torch.empty(M, N, dtype=torch.bfloat16, device=gu.device)
     xq, sx = _quant_out(M, I, gu.device, return_quant)
     lib = _lib.load()
-    nbytes = lib.fp8gq_workspace_bytes(M, N, I)
+    nbytes = _workspace_bytes(lib, gu.device, M, N, I)
     ws_buf = workspace(gu.device, nbytes) if nbytes else None
     st = lib.fp8gq_fused_swiglu_q_gemm(_ptr(gu), gu.stride(0), _ptr(Wd), Wd.stride(0), _ptr(Ws), Ws.stride(0),
                                        _ptr(out), out.stride(0), M, N, I, _ptr(xq), _ptr(sx), _ptr(ws_buf),
@@ -260,7 +275,7 @@ def fused_add_rmsnorm_gemv_quant(x: torch.Tensor, residual: torch.Tensor, norm_w
         residual_out = torch.empty(M, K, dtype=torch.bfloat16, device=x.device)
     xq, sx = _quant_out(M, K, x.device, return_quant)
     lib = _lib.load()
-    nbytes = lib.fp8gq_workspace_bytes(M, N, K)
+    nbytes = _workspace_bytes(lib, x.device, M, N, K)
     ws_buf = workspace(x.device, nbytes) if nbytes else None
     st = lib.fp8gq_fused_add_rmsnorm_gemv_quant(
         _ptr(x), x.stride(0), _ptr(residual), residual.stride(0), _ptr(norm_weight), float(eps), _ptr(Wq),
@@ -292,7 +307,7 @@ def fused_reduce_add_rmsnorm_gemv_quant(partials: torch.Tensor, residual: torch.
         residual_out = torch.empty(M, K, dtype=torch.bfloat16, device=partials.device)
     xq, sx = _quant_out(M, K, partials.device, return_quant)
     lib = _lib.load()
-    nbytes = lib.fp8gq_workspace_bytes(M, N, K)
+    nbytes = _workspace_bytes(lib, partials.device, M, N, K)
     ws_buf = workspace(partials.device, nbytes) if nbytes else None
     st = lib.fp8gq_fused_reduce_add_rmsnorm_gemv_quant(
         _ptr(partials), S, partials.stride(0), partials.stride(1), _ptr(residual), residual.stride(0),
