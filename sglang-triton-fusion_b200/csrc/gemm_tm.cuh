@@ -78,7 +78,8 @@ constexpr size_t kTmSmemBudgetSm = 228 * 1024;   // shared memory per SM
 constexpr size_t kTmSmemReservedPerCta = 1024;   // what the runtime keeps per resident CTA
 
 constexpr int kTmMaxStages = 8;     // ring depth limit (barrier arrays are sized for it)
-constexpr int kTmMaxCluster = 8;    // largest split-K cluster (portable cluster size)
+constexpr int kTmMaxCluster = 16;   // largest split-K cluster (16: B200's non-portable size)
+constexpr int kTmMaxPortableCluster = 8;   // clusters above this need the non-portable attribute
 
 // CTAs per SM the 16-token tile may run at (two MMA issue streams and two
 // pipelines per SM; its registers and TMEM columns allow it); the wider token
@@ -1048,13 +1049,31 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
             float sum[MT];
 #pragma unroll
             for (int m = 0; m < MT; ++m) sum[m] = 0.0f;
-            for (int64_t i = i_lo; i <= i_hi; ++i) {
-              const int64_t ui0 = (i * p.U) / G;
-              const int si = (ui0 / p.KB == nb) ? 0 : 1;
-              const float* pi = p.partials + ((i * 2 + si) * MT) * 128;
+            // the partials of up to kRed CTAs are loaded together (one L2 round
+            // trip per kRed rather than per CTA) and added in CTA order
+            // Every contributor after i_lo starts inside this row block (its
+            // slot 0); i_lo's slot is 0 only if its range starts at the row
+            // block's first tile.
+            constexpr int kRed = 8;
+            const int si_lo = ((i_lo * p.U) / G == first_u) ? 0 : 1;
+            for (int64_t i0 = i_lo; i0 <= i_hi; i0 += kRed) {
+              const int cnt = static_cast<int>(i_hi - i0 + 1 < kRed ? i_hi - i0 + 1 : kRed);
+              // float offset of contributor q's partial slot (< 2^32: at most 296 x 2 x 64 x 128)
+              auto off = [&](int q) {
+                const int64_t i = i0 + (q < cnt ? q : 0);
+                return static_cast<uint32_t>(((i * 2 + (i == i_lo ? si_lo : 0)) * MT) * 128 + row);
+              };
 #pragma unroll
-              for (int m = 0; m < MT; ++m)
-                if (m < p.M) sum[m] += __ldcg(pi + m * 128 + row);
+              for (int m = 0; m < MT; ++m) {
+                if (m < p.M) {
+                  float v[kRed];
+#pragma unroll
+                  for (int q = 0; q < kRed; ++q) v[q] = q < cnt ? __ldcg(p.partials + off(q) + m * 128) : 0.0f;
+#pragma unroll
+                  for (int q = 0; q < kRed; ++q)
+                    if (q < cnt) sum[m] += v[q];
+                }
+              }
             }
 #pragma unroll
             for (int m = 0; m < MT; ++m)
@@ -1116,7 +1135,7 @@ inline int tm_grid(int64_t U, int sm_count, int MT, int NB = 0, int KB = 0) {
   if (NB > 0 && KB > 0) {
     // splits a cluster can reduce (S <= 8) first: the workspace hand-off of a
     // wider split costs more than the extra CTAs gain
-    for (int max_split : {kTmMaxCluster, KB}) {
+    for (int max_split : {kTmMaxPortableCluster, KB}) {
       int64_t best = 0;
       for (int S = 1; S <= KB && S <= max_split; S *= 2)
         if (KB % S == 0 && static_cast<int64_t>(NB) * S <= slots) best = static_cast<int64_t>(NB) * S;
@@ -1284,6 +1303,22 @@ inline cudaError_t ensure_max_smem(const void* fn, int max_smem) {
   return cudaSuccess;
 }
 
+// cudaFuncAttributeNonPortableClusterSizeAllowed set once per kernel and
+// device, before a cluster of more than 8 CTAs is queried or launched.
+inline cudaError_t ensure_nonportable_clusters(const void* fn) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, bool> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_pair(dev, fn);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess) done[key] = true;
+  return e;
+}
+
 // Shared-memory plan of one pass: ring depth, activation mode and layout.
 struct TmPlan {
   int stages, npw, resident;
@@ -1351,6 +1386,8 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   if (p.norm.norm && !pl.resident) return 8;
   auto fn = gemm_tm_kernel<MT, SW>;
   if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) != cudaSuccess) return 7;  // FP8GQ_ERR_LAUNCH
+  if (csize > kTmMaxPortableCluster && ensure_nonportable_clusters(reinterpret_cast<const void*>(fn)) != cudaSuccess)
+    return 7;
   p.stages = pl.stages;
   p.npw = pl.npw;
   p.resident = pl.resident;
@@ -1377,7 +1414,8 @@ int tm_max_clusters(int csize, size_t smem, int max_smem) {
   if (it != cache.end()) return it->second;
   auto fn = gemm_tm_kernel<MT, SW>;
   int n = 0;
-  if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) == cudaSuccess) {
+  if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) == cudaSuccess &&
+      (csize <= kTmMaxPortableCluster || ensure_nonportable_clusters(reinterpret_cast<const void*>(fn)) == cudaSuccess)) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(csize);
     cfg.blockDim = dim3(kTmThreads);
@@ -1416,9 +1454,11 @@ int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem,
     if (need_resident && !pl.resident) return false;
     // one CTA per SM (the deep ring): the clusters must all fit at once.  The
     // occupancy query counts one CTA per SM, which is exact here; with two
-    // per SM (G > SMs) clusters pack twice as densely and G <= slots holds.
+    // per SM (G > SMs) clusters of up to 8 pack twice as densely and
+    // G <= slots holds.  Clusters of 16 (non-portable) are always checked.
     const bool one_per_sm = tm_ctas_per_sm<MT>() == 1 || G <= sm_count;
-    if (cluster && one_per_sm && tm_max_clusters<MT, SW>(S, pl.smem, max_smem) < NB) return false;
+    if (cluster && (one_per_sm || S > kTmMaxPortableCluster) && tm_max_clusters<MT, SW>(S, pl.smem, max_smem) < NB)
+      return false;
     return true;
   };
   int64_t best = 0;
@@ -1430,7 +1470,7 @@ int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem,
   }
   if (best > 0 && (best / NB >= 2 || best >= sm_count / 2)) return static_cast<int>(best);
   int64_t wide = 0;
-  for (int S = 2 * kTmMaxCluster; S <= KB; S *= 2) {
+  for (int S = 2 * kTmMaxPortableCluster; S <= KB; S *= 2) {
     const int64_t G = static_cast<int64_t>(NB) * S;
     if (KB % S || G > slots) continue;
     if (usable(G, false, S)) wide = G;

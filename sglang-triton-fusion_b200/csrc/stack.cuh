@@ -635,13 +635,29 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
               float sum[kStMT];
 #pragma unroll
               for (int m = 0; m < kStMT; ++m) sum[m] = 0.0f;
-              for (int64_t i = i_lo; i <= i_hi; ++i) {
-                const int64_t ui0 = (i * r.U) / r.Gl;
-                const int si = (ui0 / r.KB == nb) ? 0 : 1;
-                const float* pi = p.partials + (((static_cast<int64_t>(bank) * G + i) * 2 + si) * M) * 128;
+              // the partials of up to 8 CTAs are loaded together and added
+              // in CTA order
+              const int si_lo = ((i_lo * r.U) / r.Gl == first_u) ? 0 : 1;
+              for (int64_t i0 = i_lo; i0 <= i_hi; i0 += 8) {
+                const int cnt = static_cast<int>(i_hi - i0 + 1 < 8 ? i_hi - i0 + 1 : 8);
+                // float offset of contributor q's partial slot (< 2^32: 2 x 148 x 2 x 16 x 128);
+                // every contributor after i_lo starts inside this row block (slot 0)
+                auto off = [&](int q) {
+                  const int64_t i = i0 + (q < cnt ? q : 0);
+                  return static_cast<uint32_t>(
+                      (((static_cast<int64_t>(bank) * G + i) * 2 + (i == i_lo ? si_lo : 0)) * M) * 128 + row);
+                };
 #pragma unroll
-                for (int m = 0; m < kStMT; ++m)
-                  if (m < M) sum[m] += __ldcg(pi + m * 128 + row);
+                for (int m = 0; m < kStMT; ++m) {
+                  if (m < M) {
+                    float v[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) v[q] = q < cnt ? __ldcg(p.partials + off(q) + m * 128) : 0.0f;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                      if (q < cnt) sum[m] += v[q];
+                  }
+                }
               }
 #pragma unroll
               for (int m = 0; m < kStMT; ++m)
