@@ -7,7 +7,10 @@ gate_up 4096->24576, down 12288->4096 -- for each of 36 layers, every layer
 with its own seeded random e4m3 weights and 128x128 fp32 block scales
 (W ~ N(0, 0.02^2) block-quantised, activations bf16 ~ N(0, 1) with 1% of the
 channels x20).  6.95 GB of weights per step, far larger than the 126 MB L2,
-so no L2 flush is needed between steps.  With --gpus N > 1 the weights are
+so no L2 flush is needed between steps.  The weights are declared static
+(fp8gq.set_static_weights; --static-weights 0 turns it off): nothing in a
+decode step writes them, so each kernel may fetch its first weight tiles
+before the previous kernel in the stream has finished.  With --gpus N > 1 the weights are
 sharded across the ranks, so the total work is fixed (strong scaling):
 --tp-mode paired makes qkv and gate_up column-parallel and o and
 down row-parallel, the row-parallel kernels storing their partial outputs
@@ -88,9 +91,10 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--e2e-steps", type=int, default=100)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--static-weights", type=int, default=0,
-                    help="1: declare the weights static (fp8gq.set_static_weights), letting each "
-                         "kernel prefetch its first weight tiles before the previous one finishes")
+    ap.add_argument("--static-weights", type=int, default=1,
+                    help="1 (default): declare the weights static (fp8gq.set_static_weights) -- no work "
+                         "queued before a linear writes its weights, as in any decode step -- letting each "
+                         "kernel fetch its first weight tiles before the previous one finishes; 0: do not")
     ap.add_argument("--tp-mode", choices=["paired", "gather", "nccl"], default="gather",
                     help="N > 1: paired -- qkv and gate_up column-parallel, o and down "
                          "row-parallel; each row-parallel kernel stores its partial into every rank's "
@@ -102,8 +106,9 @@ def parse():
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
                          "norm_<shape> (add + RMSNorm prologue), writer, add_rmsnorm, group_quant "
-                         "(activation kernels alone, M rows), or 'stack' for the whole decode step's "
-                         "routed linears")
+                         "(activation kernels alone, M rows), 'stack' for the whole decode step's "
+                         "routed linears, or 'stack_runner[:L=<layers>]' for the decode chain in one "
+                         "persistent launch")
     return ap.parse_args()
 
 
