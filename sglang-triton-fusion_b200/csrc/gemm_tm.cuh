@@ -1123,28 +1123,6 @@ inline int tm_token_tile(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 // Resident CTA slots for the token tile (the most CTAs one launch may use).
 inline int tm_slots(int sm_count, int MT) { return sm_count * (MT == 16 ? tm_ctas_per_sm<16>() : 1); }
 
-// Grid size.  Preferred: an aligned split -- every CTA takes one row block's
-// K range cut in S equal parts (S a power of two dividing K/128), so the
-// split-K hand-off involves only the S CTAs of a row block (a cluster when
-// S <= 8) and S = 1 needs none -- with NB * S the largest such count that
-// fits the resident CTA slots (measured on B200: with the cluster hand-off,
-// two CTAs per SM with short K runs beat one with long runs), splits of at
-// most 8 preferred.  Otherwise stream-K over all resident slots.
-inline int tm_grid(int64_t U, int sm_count, int MT, int NB = 0, int KB = 0) {
-  const int64_t slots = tm_slots(sm_count, MT);
-  if (NB > 0 && KB > 0) {
-    // splits a cluster can reduce (S <= 8) first: the workspace hand-off of a
-    // wider split costs more than the extra CTAs gain
-    for (int max_split : {kTmMaxPortableCluster, KB}) {
-      int64_t best = 0;
-      for (int S = 1; S <= KB && S <= max_split; S *= 2)
-        if (KB % S == 0 && static_cast<int64_t>(NB) * S <= slots) best = static_cast<int64_t>(NB) * S;
-      if (best >= sm_count / 2) return static_cast<int>(best);
-    }
-  }
-  return static_cast<int>(U < slots ? U : slots);
-}
-
 // Whether M tokens may take the pre-quantised feed: every pass has one K
 // block per accumulator group (16-token tile with M > 8, or a wider tile).
 // The pre-quantised feed may serve any M (the workspace then holds the
@@ -1434,14 +1412,20 @@ int tm_max_clusters(int csize, size_t smem, int max_smem) {
   return n;
 }
 
-// Grid of a launch.  First choice: the widest aligned split S <= 8 (the S
-// CTAs of a row block share its K range and reduce in a cluster) whose grid
-// fits the resident CTA slots and whose clusters are all resident in one wave
-// (measured on B200: a second wave of clusters, e.g. 16 clusters of 8
-// one-per-SM CTAs where 15 fit, costs more than a narrower split).  Wider splits hand off
-// through the workspace and stream-K spreads the tiles over all slots; both
-// only when no cluster split of at least 2 (or with half the SMs) exists.
-// With need_resident, only grids whose plan keeps the activation resident.
+// Grid of a launch.  First choice: the widest aligned split -- the S CTAs of
+// a row block share its K range (any 1 <= S <= min(KB, 16); the K blocks
+// split as evenly as the integers allow) and reduce in a cluster -- whose
+// grid fits the resident CTA slots and whose clusters are all resident in one
+// wave (measured on B200: a second wave, e.g. 16 clusters of 8 one-per-SM
+// CTAs where 15 fit, costs more than a narrower split).  The occupancy query
+// counts one CTA per SM; a grid above the SM count runs two CTAs per SM, where
+// a cluster of S CTAs needs ceil(S/2) SMs, so its capacity is the query's for
+// clusters of ceil(S/2) (measured: 2048 x 12288 at M = 1 takes 9.9 us with 16
+// clusters of 12 at two per SM against 13.3 us with 16 clusters of 4 at one).
+// Wider splits hand off through the workspace and stream-K spreads the tiles
+// over all slots; both only when no cluster split of at least 2 (or with half
+// the SMs) exists.  With need_resident, only grids whose plan keeps the
+// activation resident.
 template <int MT, bool SW>
 int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem, int resident_mode,
                    bool need_resident, int64_t extra_tail) {
@@ -1452,19 +1436,15 @@ int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem,
     if (!tm_plan<MT, SW>(&pl, mp, U, KB, static_cast<int>(G), sm_count, max_smem, resident_mode, extra_tail))
       return false;
     if (need_resident && !pl.resident) return false;
-    // one CTA per SM (the deep ring): the clusters must all fit at once.  The
-    // occupancy query counts one CTA per SM, which is exact here; with two
-    // per SM (G > SMs) clusters of up to 8 pack twice as densely and
-    // G <= slots holds.  Clusters of 16 (non-portable) are always checked.
+    if (!cluster) return true;
     const bool one_per_sm = tm_ctas_per_sm<MT>() == 1 || G <= sm_count;
-    if (cluster && (one_per_sm || S > kTmMaxPortableCluster) && tm_max_clusters<MT, SW>(S, pl.smem, max_smem) < NB)
-      return false;
-    return true;
+    const int span = one_per_sm ? S : (S + 1) / 2;      // SMs a cluster occupies
+    return span < 2 || tm_max_clusters<MT, SW>(span, pl.smem, max_smem) >= NB;
   };
   int64_t best = 0;
-  for (int S = 1; S <= KB && S <= kTmMaxCluster; S *= 2) {
+  for (int S = 1; S <= KB && S <= kTmMaxCluster; ++S) {
     const int64_t G = static_cast<int64_t>(NB) * S;
-    if (KB % S || G > slots) continue;
+    if (G > slots) break;
     // (the same grid whichever hand-off runs, so the results do not depend on it)
     if (usable(G, S > 1, S)) best = G;
   }
@@ -1543,7 +1523,11 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   // aligned split: every CTA takes 1/split of one row block's K range
   const int NB = N / kGroup;
   const int split = (grid % NB == 0) ? grid / NB : 0;
-  const bool aligned = split > 0 && p.KB % split == 0;
+  // (any split works: with G = NB * split, CTA i's stream-K range
+  // [i*U/G, (i+1)*U/G) starts at row block i / split's first tile exactly when
+  // i is a multiple of split, so the split CTAs of a row block cover it
+  // alone, with floor(KB/split) or ceil(KB/split) K blocks each)
+  const bool aligned = split > 0 && split <= p.KB;
   const int csize = (cluster_mode != 0 && aligned && split >= 2 && split <= kTmMaxCluster) ? split : 1;
   const int64_t xcols = swiglu ? 2 * static_cast<int64_t>(K) : K;
   // Pre-quantised feed: large M whose activation does not stay resident at
