@@ -215,12 +215,12 @@ def test_tile_kernel_strides_and_determinism(fp8gq, cuda_device):
     (1, 4096, 24576, False),    # one CTA per row block, whole K range resident (slot = K block)
     (1, 4096, 4096, False),     # K range split 8 ways: a cluster of 8 CTAs per row block (slot = tile)
     (2, 4096, 6144, False),     # a cluster of 4
-    (3, 2560, 4096, False),
+    (3, 2560, 4096, False),     # 20 K blocks over clusters of 8: uneven K ranges (2 or 3 K blocks)
     (4, 4096, 1152, False),     # 9 row blocks: a cluster of 8 per row block, one CTA per SM
     (1, 12288, 512, False),     # 4 row blocks x 96 K blocks: a cluster of 16 (non-portable) per row block
     (3, 12288, 1024, False),    # 8 row blocks: clusters of 16 where they all fit, else of 8
     (4, 4096, 512, True),       # SwiGLU with a cluster of 16
-    (2, 10368, 896, False),     # stream-K: CTA ranges cross row blocks, K blocks wrap
+    (2, 10368, 896, False),     # 7 row blocks x 81 K blocks: clusters of 16 with uneven K ranges
     (16, 1024, 1280, False),    # 16 tokens x 8 K blocks: a large resident footprint
     (16, 4096, 6144, False),    # 16 tokens x 8 K blocks per CTA: the resident feed fits
     (16, 4096, 24576, False),   # 16 tokens x 32 K blocks: only the pre-quantised feed fits
