@@ -1427,8 +1427,8 @@ int tm_max_clusters(int csize, size_t smem, int max_smem) {
 // the SMs) exists.  With need_resident, only grids whose plan keeps the
 // activation resident.
 template <int MT, bool SW>
-int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem, int resident_mode,
-                   bool need_resident, int64_t extra_tail) {
+int tm_choose_grid_uncached(int NB, int KB, int64_t U, int M, int sm_count, int max_smem, int resident_mode,
+                            bool need_resident, int64_t extra_tail) {
   const int64_t slots = tm_slots(sm_count, MT);
   const int mp = M < MT ? M : MT;
   auto usable = [&](int64_t G, bool cluster, int S) {
@@ -1459,6 +1459,30 @@ int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem,
   for (int64_t G : {U < slots ? U : slots, U < sm_count ? U : static_cast<int64_t>(sm_count)})
     if (usable(G, false, 1)) return static_cast<int>(G);
   return best > 0 ? static_cast<int>(best) : 0;
+}
+
+// tm_choose_grid_uncached, remembered per device and argument set (a decode
+// loop asks for the same few shapes on every call).
+template <int MT, bool SW>
+int tm_choose_grid(int NB, int KB, int64_t U, int M, int sm_count, int max_smem, int resident_mode,
+                   bool need_resident, int64_t extra_tail) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, int, int, int, int64_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const int mp = M < MT ? M : MT;
+  const auto key = std::make_tuple(dev, NB, KB, mp, max_smem, resident_mode, need_resident ? 1 : 0, extra_tail);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  const int g = tm_choose_grid_uncached<MT, SW>(NB, KB, U, M, sm_count, max_smem, resident_mode, need_resident,
+                                                extra_tail);
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache.size() >= kTmapCacheMax) cache.clear();
+  cache.emplace(key, g);
+  return g;
 }
 
 // Runs ceil(M / MT) passes of at most MT tokens; every pass reuses the

@@ -173,17 +173,17 @@ class PeerGather:
                wait_input: bool = True, desc=None):
         """out[:, rank*Nr:(rank+1)*Nr] = fused_gemv_quant(x, Wq_shard, Ws_shard) on every rank."""
         M, K = x.shape
-        Nr = Wq_shard.shape[0]
-        ops._check_weight(Wq_shard, Ws_shard, K)
+        Nr, ldw, ldws = ops._check_weight_strides(Wq_shard, Ws_shard, K)
         if out.shape != (M, Nr * self.world):
             raise ops.ShapeError(f"out must be [{M}, {Nr * self.world}], got {tuple(out.shape)}")
         g = desc if desc is not None else self.descriptor(out, self.rank * Nr, wait_input)
-        nbytes = ops._workspace_bytes(self.lib, x.device, M, Nr, K)
-        ws_buf = ops.workspace(x.device, nbytes) if nbytes else None
+        dev = x.device
+        stream = ops._stream(dev)
+        nbytes = ops._workspace_bytes(self.lib, dev, M, Nr, K)
+        ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, stream)[1:] if nbytes else (None, 0)
         st = self.lib.fp8gq_fused_gemv_quant_gather(
-            x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), Wq_shard.stride(0), Ws_shard.data_ptr(),
-            Ws_shard.stride(0), M, Nr, K, ctypes.byref(g), None if ws_buf is None else ws_buf.data_ptr(),
-            0 if ws_buf is None else ws_buf.numel(), ops._stream(x.device))
+            x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), ldw, Ws_shard.data_ptr(), ldws, M, Nr, K,
+            ctypes.byref(g), ws_ptr, ws_n, stream)
         _lib.check(st, "fp8gq_fused_gemv_quant_gather")
         return out
 
@@ -227,14 +227,15 @@ class PeerGather:
                 raise ops.ShapeError(f"gu must be [M, {2 * Kr}], got {tuple(x.shape)}")
         elif x.shape[1] != Kr:
             raise ops.ShapeError(f"x must be [M, {Kr}], got {tuple(x.shape)}")
-        ops._check_weight(Wq_cols, Ws_cols, Kr)
+        _, ldw, ldws = ops._check_weight_strides(Wq_cols, Ws_cols, Kr)
         g = desc if desc is not None else self.partial_descriptor(slabs)
-        nbytes = ops._workspace_bytes(self.lib, x.device, M, N, Kr)
-        ws_buf = ops.workspace(x.device, nbytes) if nbytes else None
+        dev = x.device
+        stream = ops._stream(dev)
+        nbytes = ops._workspace_bytes(self.lib, dev, M, N, Kr)
+        ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, stream)[1:] if nbytes else (None, 0)
         fn = self.lib.fp8gq_fused_swiglu_q_gemm_gather if swiglu else self.lib.fp8gq_fused_gemv_quant_gather
-        st = fn(x.data_ptr(), x.stride(0), Wq_cols.data_ptr(), Wq_cols.stride(0), Ws_cols.data_ptr(),
-                Ws_cols.stride(0), M, N, Kr, ctypes.byref(g), None if ws_buf is None else ws_buf.data_ptr(),
-                0 if ws_buf is None else ws_buf.numel(), ops._stream(x.device))
+        st = fn(x.data_ptr(), x.stride(0), Wq_cols.data_ptr(), ldw, Ws_cols.data_ptr(), ldws, M, N, Kr,
+                ctypes.byref(g), ws_ptr, ws_n, stream)
         _lib.check(st, "fp8gq_fused_swiglu_q_gemm_gather" if swiglu else "fp8gq_fused_gemv_quant_gather")
         return slabs
 

@@ -55,12 +55,20 @@ def workspace(device: torch.device, nbytes: int, stream: int | None = None) -> t
     (and warm every shape up) before capturing a CUDA graph."""
     if stream is None:
         stream = _stream(device)
+    return _workspace_entry(device, nbytes, stream)[0]
+
+
+def _workspace_entry(device: torch.device, nbytes: int, stream: int):
+    """(tensor, address, bytes) of the scratch of (device, stream), at least
+    nbytes; the address and size are kept so that a call needs no tensor
+    method to pass them."""
     key = (device.index, stream)
-    buf = _workspaces.get(key)
-    if buf is None or buf.numel() < nbytes:
+    ent = _workspaces.get(key)
+    if ent is None or ent[2] < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _workspaces[key] = buf
-    return buf
+        ent = (buf, buf.data_ptr(), buf.numel())
+        _workspaces[key] = ent
+    return ent
 
 
 def _check_cuda(*ts):
@@ -70,6 +78,12 @@ def _check_cuda(*ts):
 
 
 def _check_weight(Wq: torch.Tensor, Ws: torch.Tensor, K: int):
+    """Checks a weight and its block scales against K; returns N."""
+    return _check_weight_strides(Wq, Ws, K)[0]
+
+
+def _check_weight_strides(Wq: torch.Tensor, Ws: torch.Tensor, K: int):
+    """_check_weight, also returning the row strides: (N, ldw, ldws)."""
     if Wq.dtype != torch.float8_e4m3fn:
         raise TypeError(f"weight must be float8_e4m3fn, got {Wq.dtype}")
     if Ws.dtype != torch.float32:
@@ -79,11 +93,13 @@ def _check_weight(Wq: torch.Tensor, Ws: torch.Tensor, K: int):
         raise ShapeError(f"weight has K={Kw}, activation has K={K}")
     if K % GROUP or N % GROUP:
         raise ShapeError("K and N must be multiples of 128")
-    if Wq.stride(1) != 1 or Ws.stride(1) != 1:
+    ws_t = Wq.stride()
+    ss_t = Ws.stride()
+    if ws_t[1] != 1 or ss_t[1] != 1:
         raise ValueError("weight and weight_scale must be contiguous along K")
-    if tuple(Ws.shape) != (N // GROUP, K // GROUP):
+    if Ws.shape != (N // GROUP, K // GROUP):
         raise ShapeError(f"weight_scale must be [{N // GROUP}, {K // GROUP}], got {tuple(Ws.shape)}")
-    return N
+    return N, ws_t[0], ss_t[0]
 
 
 def _quant_out(M, K, device, want):
@@ -106,28 +122,30 @@ def fused_gemv_quant(x: torch.Tensor, Wq: torch.Tensor, Ws: torch.Tensor, *, out
     if x.dtype != torch.bfloat16 or x.dim() != 2:
         raise TypeError("x must be a 2-D bf16 tensor")
     M, K = x.shape
-    N = _check_weight(Wq, Ws, K)
-    if x.stride(1) != 1:
+    N, ldw, ldws = _check_weight_strides(Wq, Ws, K)
+    xs = x.stride()
+    if xs[1] != 1:
         raise ValueError("x must be contiguous along K")
+    dev = x.device
     if out is None:
-        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    xq, sx = _quant_out(M, K, x.device, return_quant)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    xq, sx = _quant_out(M, K, dev, return_quant)
     lib = _lib.load()
-    stream = _stream(x.device)
+    stream = _stream(dev)
     if kernel == "row":
         if M != 1:
             raise ShapeError("the row kernel takes M == 1")
-        st = lib.fp8gq_gemv_quant_row(_ptr(x), _ptr(Wq), Wq.stride(0), _ptr(Ws), Ws.stride(0), _ptr(out),
+        st = lib.fp8gq_gemv_quant_row(x.data_ptr(), Wq.data_ptr(), ldw, Ws.data_ptr(), ldws, out.data_ptr(),
                                       N, K, _ptr(xq), _ptr(sx), stream)
         _lib.check(st, "fp8gq_gemv_quant_row")
     else:
-        nbytes = _workspace_bytes(lib, x.device, M, N, K, tile_only=kernel != "auto")
-        ws_buf = workspace(x.device, nbytes, stream) if nbytes else None
-        fn = lib.fp8gq_fused_gemv_quant if kernel == "auto" else lib.fp8gq_gemv_quant_tm
         if kernel not in ("auto", "tm"):
             raise ValueError(f"unknown kernel {kernel!r}")
-        st = fn(_ptr(x), x.stride(0), _ptr(Wq), Wq.stride(0), _ptr(Ws), Ws.stride(0), _ptr(out), out.stride(0),
-                M, N, K, _ptr(xq), _ptr(sx), _ptr(ws_buf), 0 if ws_buf is None else ws_buf.numel(), stream)
+        nbytes = _workspace_bytes(lib, dev, M, N, K, tile_only=kernel != "auto")
+        ws_ptr, ws_n = _workspace_entry(dev, nbytes, stream)[1:] if nbytes else (None, 0)
+        fn = lib.fp8gq_fused_gemv_quant if kernel == "auto" else lib.fp8gq_gemv_quant_tm
+        st = fn(x.data_ptr(), xs[0], Wq.data_ptr(), ldw, Ws.data_ptr(), ldws, out.data_ptr(), out.stride(0),
+                M, N, K, _ptr(xq), _ptr(sx), ws_ptr, ws_n, stream)
         _lib.check(st, fn.__name__)
     return (out, xq, sx) if return_quant else out
 
