@@ -10,8 +10,8 @@
 // weights that is a third of the time.  Here the weights of the next linear
 // do not depend on anything: each CTA's TMA warp runs straight on into the
 // next linear's weight tiles while the same CTA's MMAs still wait for that
-// linear's activation, so the ring (up to 12 stages of 16 KB per SM) keeps
-// HBM busy across the dependency.
+// linear's activation, so the ring (8 stages of 16 KB per SM) keeps HBM busy
+// across the dependency.
 //
 // Dependencies.  Linear l reads its activation only once every CTA has
 // finished linear dep(l) (the latest earlier linear whose output overlaps
@@ -33,9 +33,13 @@
 // Token layout, MMA, TMEM groups and epilogue scaling are the tile kernel's
 // (swap-AB tcgen05 kind::f8f6f4, 128 weight rows x 16 token columns, K blocks
 // of a group side by side in a 16-column accumulator, per-(token, K block)
-// scale sx * ws applied in the epilogue).  The activation warps quantise each
-// K block straight from global memory (the activation is a few KB, in L2)
-// into the stage's B tile and put its scales in a ring the epilogue reads.
+// scale sx * ws applied in the epilogue).  Per linear, the activation warps
+// load the block scales of the CTA's tiles, wait for the linear's dependency,
+// and quantise the activation of the CTA's K blocks once into shared memory
+// (the activation is a few KB, in L2); each stage's B tile is then a copy of
+// prebuilt bytes, and the tile's scales go into a ring the epilogue reads.
+// Where M x (K blocks) does not fit the resident region, the owning warp
+// quantises each K block from global memory instead.
 //
 // Warp roles (320 threads): warp 0 TMA producer (weights only), warp 1 TMEM
 // allocator and MMA issuer, warps 2-5 activation producers, warps 6-9

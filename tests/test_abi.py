@@ -97,3 +97,29 @@ def test_fp8gq_error_carries_status():
     from fp8gq._lib import Fp8gqError
     e = Fp8gqError(3, "fp8gq_gemv_quant_row")
     assert e.status == 3 and "FP8GQ_ERR_ALIGNMENT" in str(e)
+
+
+def test_weight_checks_and_strides():
+    """The host-side weight checks of every op (CPU tensors: no device is
+    touched): dtypes, K against the activation, multiples of 128, contiguity
+    along K, the scale shape; and the row strides they return."""
+    import torch
+    from fp8gq import ops
+    w = torch.zeros(256, 384, dtype=torch.float8_e4m3fn)
+    s = torch.ones(2, 3)
+    assert ops._check_weight_strides(w, s, 384) == (256, 384, 3)
+    wide = torch.zeros(256, 512, dtype=torch.float8_e4m3fn)[:, :384]          # row stride 512
+    assert ops._check_weight_strides(wide, s, 384) == (256, 512, 3)
+    assert ops._check_weight(w, s, 384) == 256
+    with pytest.raises(TypeError):
+        ops._check_weight_strides(w.view(torch.uint8), s, 384)
+    with pytest.raises(TypeError):
+        ops._check_weight_strides(w, s.double(), 384)
+    with pytest.raises(ops.ShapeError):
+        ops._check_weight_strides(w, s, 256)                                     # K mismatch
+    with pytest.raises(ops.ShapeError):
+        ops._check_weight_strides(torch.zeros(200, 384, dtype=torch.float8_e4m3fn), s, 384)
+    with pytest.raises(ValueError):
+        ops._check_weight_strides(torch.zeros(384, 256, dtype=torch.float8_e4m3fn).t(), s, 384)
+    with pytest.raises(ops.ShapeError):
+        ops._check_weight_strides(w, torch.ones(2, 2), 384)                       # scale shape
