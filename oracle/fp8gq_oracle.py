@@ -402,7 +402,7 @@ def ref_atol(ref: np.ndarray, ulps: float) -> float:
     return ulps * bf16_ulp_at(float(np.abs(ref).max())) + 1e-3
 
 
-def north_star_ok(got: np.ndarray, ref: np.ndarray, rtol: float = 1e-2, atol_rel_rms: float = 1e-2):
+def rms_tolerance_ok(got: np.ndarray, ref: np.ndarray, rtol: float = 1e-2, atol_rel_rms: float = 1e-2):
     """|got - ref| <= rtol*|ref| + atol_rel_rms * RMS(ref), elementwise."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)

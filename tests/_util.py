@@ -38,10 +38,10 @@ def ulp_report(got: np.ndarray, ref: np.ndarray) -> str:
 
 
 def assert_close(got, ref_exact, ulps: float):
-    """Both tolerances: the north star's (rtol 1e-2, atol 1e-2 * RMS) and the
+    """Both tolerances: the relative one (rtol 1e-2, atol 1e-2 * RMS) and the
     reference self-test's (atol = ulps * ulp_bf16(max|ref|) + 1e-3, rtol 0)."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref_exact, np.float64)
-    assert O.north_star_ok(got, ref), "north-star tolerance: " + ulp_report(got, ref)
+    assert O.rms_tolerance_ok(got, ref), "rtol 1e-2 / atol 1e-2*RMS tolerance: " + ulp_report(got, ref)
     atol = O.ref_atol(ref, ulps)
     assert np.all(np.abs(got - ref) <= atol), f"reference tolerance {ulps} ulp: " + ulp_report(got, ref)

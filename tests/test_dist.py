@@ -152,7 +152,7 @@ def _paired_worker(rank, world, port, q):
         gu_full, _, _, _, r1f = O.fused_add_rmsnorm_gemv_quant(o_full, res0, nw, wgu, sgu)
         d_full, _, _, _ = O.fused_swiglu_q_gemm(gu_full, wd, sd)
         h2f, _, _ = O.add_rmsnorm(d_full, r1f, nw)
-        q.put((rank, bool(O.north_star_ok(h2, h2f, rtol=5e-2, atol_rel_rms=5e-2)),
+        q.put((rank, bool(O.rms_tolerance_ok(h2, h2f, rtol=5e-2, atol_rel_rms=5e-2)),
                float(np.abs(h2 - h2f).max()), bool(np.array_equal(res1, allgather(res1)[0]))))
     finally:
         dist.destroy_process_group()

@@ -1,6 +1,6 @@
 """Parity of the CUDA kernels (through the C ABI, via fp8gq.ops) against the
 CPU oracle: quantised activation bytes and scales bit-exact, outputs within
-the north star's tolerance (rtol 1e-2, atol 1e-2 * RMS) and within the
+a relative tolerance (rtol 1e-2, atol 1e-2 * RMS) and within the
 reference self-tests' ulp tolerance (2 bf16 ulp + 1e-3 for the row and
 SwiGLU kernels, kernels/fused_gemv_quant.py:107-108; 3 ulp + 1e-3 for the
 tile kernel, kernels/fused_gemv_quant_tm.py:138-140)."""
@@ -19,7 +19,7 @@ pytestmark = pytest.mark.gpu
 GOLDEN = sorted(p for p in (Path(__file__).parent / "golden").glob("*.npz") if not p.stem.startswith("writer_"))
 WRITER_GOLDEN = sorted((Path(__file__).parent / "golden").glob("writer_*.npz"))
 
-# Qwen3-8B decode linears (K, N) and Qwen3-4B tile shapes
+# the Qwen3-8B decode linears (K, N) and the Qwen3-4B small-batch shapes
 QWEN3_8B = {"qkv": (4096, 6144), "o": (4096, 4096), "gate_up": (4096, 24576), "down": (12288, 4096)}
 QWEN3_4B = {"q": (2560, 4096), "gate_up": (2560, 19456), "down": (9728, 2560)}
 
