@@ -122,49 +122,74 @@ def measured_peak():
 
 # ------------------------------------------------------------- clocks --
 class ClockSampler:
-    """nvidia-smi samples of the GPU this rank runs on, during the timed region."""
+    """nvidia-smi samples of the job's GPUs (every rank's, identified by UUID),
+    taken by one process on rank 0 while the GPUs run the step.  The timed
+    region of a short run lasts milliseconds, less than the sampling period,
+    so the bench keeps replaying the same step for a load window around it
+    (untimed replays before and after) and the sampler covers that window;
+    __enter__ returns once the first sample has arrived."""
 
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuid: str | None):
-        self.uuid = uuid
+    def __init__(self, uuids, active: bool = True):
+        self.uuids = [u for u in (uuids or []) if u]
+        self.active = active
         self.proc = None
+        self.lines = []
+        self.marks = []
+
+    def _reader(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
 
     def __enter__(self):
+        import threading
+        if not self.active:
+            return self
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        threading.Thread(target=self._reader, daemon=True).start()
+        t0 = time.monotonic()
+        while not self.lines and time.monotonic() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.02)
         return self
 
+    def mark(self):
+        """Start (first call) and end (second call) of the loaded window."""
+        self.marks.append(time.monotonic())
+
     def __exit__(self, *exc):
-        self.out = ""
         if self.proc is not None:
             self.proc.terminate()
             try:
-                self.out, _ = self.proc.communicate(timeout=10)
+                self.proc.wait(timeout=10)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                self.out, _ = self.proc.communicate()
 
     def summary(self):
+        lo, hi = (self.marks + [float("inf")] * 2)[:2] if self.marks else (float("-inf"), float("inf"))
         rows = []
-        for line in (self.out or "").splitlines():
+        for t, line in self.lines:
+            if not lo <= t <= hi:
+                continue
             f = [c.strip() for c in line.split(",")]
             if len(f) < 9:
                 continue
-            if self.uuid and self.uuid not in f[0]:
+            if self.uuids and not any(u in f[0] or f[0] in u for u in self.uuids):
                 continue
             try:
                 rows.append((float(f[1]), float(f[2]), f[4], f[5], f[6], f[7], f[8]))
             except ValueError:
                 continue
         if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
         reasons = set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -172,7 +197,8 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows), "gpus": len(self.uuids) or None,
+                "window": "untimed replays of the same step around the timed region"}
 
 
 # ---------------------------------------------------------- CPU path --
@@ -272,6 +298,51 @@ def decode_chain(layers, dev, M=1):
                  fp8gq.Linear(o, wgu, sgu, gu), fp8gq.Linear(gu, wd, sd, d, swiglu=True)]
         x = d
     return lins, h
+
+
+def layer_parity(layer, world, rank, dev):
+    """Checks one layer's gathered outputs on every rank against the oracle of
+    the UNSHARDED linears (a checker only, outside every timed region): rank r
+    holds rows [r*N/w, (r+1)*N/w) of each weight, so the full weight is the
+    ranks' shards in rank order.  Rank 0 evaluates the oracle (CPU, float64)
+    on that full weight and the layer's input; every rank then compares its own
+    full output with it (the tile kernel's tolerance: 3 bf16 ulp of max |ref| +
+    1e-3, and rtol 1e-2 / atol 1e-2 * RMS) and with rank 0's copy bit for bit."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from oracle import fp8gq_oracle as O
+    ok, worst, same = True, 0.0, True
+    for name, K, N, wq, ws, x, out, shard in layer:
+        if world > 1:
+            wfull = torch.empty(N, K, dtype=torch.uint8, device=dev)
+            sfull = torch.empty(N // 128, K // 128, dtype=torch.float32, device=dev)
+            dist.all_gather_into_tensor(wfull, wq.view(torch.uint8).contiguous())
+            dist.all_gather_into_tensor(sfull, ws.contiguous())
+        else:
+            wfull, sfull = wq.view(torch.uint8), ws
+        exact = torch.zeros(1, N, dtype=torch.float64, device=dev)
+        if rank == 0:
+            _, ex, _, _ = O.fused_gemv_quant(x.float().cpu().numpy(), wfull.cpu().numpy(), sfull.cpu().numpy())
+            exact.copy_(torch.from_numpy(ex))
+        ref0 = out.clone()
+        if world > 1:
+            dist.broadcast(exact, src=0)
+            dist.broadcast(ref0, src=0)
+        ex = exact.cpu().numpy()
+        got = out.float().cpu().numpy().astype(np.float64)
+        atol = O.ref_atol(ex, 3.0)
+        ok = ok and bool(O.rms_tolerance_ok(got, ex)) and bool(np.all(np.abs(got - ex) <= atol))
+        worst = max(worst, float(np.abs(got - ex).max() / O.bf16_ulp_at(float(np.abs(ex).max()))))
+        same = same and torch.equal(ref0, out)
+    flags = torch.tensor([1.0 if ok else 0.0, 1.0 if same else 0.0, -worst], device=dev)
+    if world > 1:
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    return {"linears": len(layer), "ok": bool(flags[0].item() == 1.0 and flags[1].item() == 1.0),
+            "within_tolerance": bool(flags[0].item() == 1.0), "ranks_identical": bool(flags[1].item() == 1.0),
+            "max_err_ulp": round(-float(flags[2].item()), 3), "ranks_checked": world,
+            "against": "oracle of the unsharded linears (CPU, float64), layer 0 of the step, 3 bf16 ulp + "
+                       "rtol 1e-2 / atol 1e-2*RMS"}
 
 
 def stack_runner_line(layers, dev, graph_us):
@@ -423,9 +494,58 @@ def run_ours(args):
         if pg is not None:
             pg.wait(layers[-1][-1][6])      # the step ends when the last slices have landed
 
+    def prepared_step_list():
+        """The same step as prepared launches (fp8gq.prepared): every call
+        recorded once, the whole step issued by one C call per run.  None for
+        the NCCL mode (its all-gathers are not library launches)."""
+        plans = []
+        if paired:
+            for L, lin in enumerate(layers):
+                (_, _, _, wqkv, sqkv, _, _, qkv_o), (_, _, _, wo, so, _, _, _), \
+                    (_, _, _, wgu, sgu, _, _, gu_o), (_, _, _, wd, sd, _, _, _) = lin
+                if L == 0:
+                    plans.append(fp8gq.prepare_fused_add_rmsnorm_gemv_quant(
+                        h_in, res_buf[0, 1], norm_w, wqkv, sqkv, out=qkv_o, residual_out=res_buf[1, 0]))
+                else:
+                    plans.append(pg.prepare_reduce_norm_linear(slabs[L - 1, 1], res_buf[L, 1], norm_w, wqkv, sqkv,
+                                                               qkv_o, res_buf[L + 1, 0], desc=wdesc))
+                plans.append(pg.prepare_linear_partial(qkv_o[:, :q_cols], wo, so, slabs[L, 0], desc=pdesc[L][0]))
+                plans.append(pg.prepare_reduce_norm_linear(slabs[L, 0], res_buf[L + 1, 0], norm_w, wgu, sgu, gu_o,
+                                                           res_buf[L + 1, 1], desc=wdesc))
+                plans.append(pg.prepare_linear_partial(gu_o, wd, sd, slabs[L, 1], swiglu=True, desc=pdesc[L][1]))
+            plans.append(pg.prepare_wait(slabs[LAYERS - 1, 1, rank]))
+        elif world == 1:
+            for lin in layers:
+                for (name, K, N, wq, ws, x, out, shard) in lin:
+                    plans.append(fp8gq.prepare_fused_gemv_quant(x, wq, ws, out=out))
+        elif pg is not None:
+            for li, lin in enumerate(layers):
+                for i, (name, K, N, wq, ws, x, out, shard) in enumerate(lin):
+                    plans.append(pg.prepare_linear(x, wq, ws, out, desc=descs[li][i]))
+            plans.append(pg.prepare_wait(layers[-1][-1][6]))
+        else:
+            return None
+        return fp8gq.LaunchList(plans)
+
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
+    barrier()
+    # the prepared form of the step must leave the same outputs as the calls
+    prepared = prepared_step_list()
+    prepared_same = None
+    if prepared is not None:
+        final = [t.clone() for t in ([res_buf, slab_buf] if paired else [out_all])]
+        prepared.run()
+        torch.cuda.synchronize()
+        barrier()
+        prepared_same = all(torch.equal(a, b) for a, b in zip(final, [res_buf, slab_buf] if paired else [out_all]))
+        if world > 1:
+            f = torch.tensor([1.0 if prepared_same else 0.0], device=dev)
+            dist.all_reduce(f, op=dist.ReduceOp.MIN)
+            prepared_same = bool(f.item() == 1.0)
+    # the outputs of the warm-up steps, checked before anything is timed
+    parity = None if paired else layer_parity(layers[0], world, rank, dev)
     barrier()
 
     graph = torch.cuda.CUDAGraph()
@@ -441,19 +561,43 @@ def run_ours(args):
         uuid = str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
         pass
+    uuids = [uuid]
+    if world > 1:
+        uuids = [None] * world
+        dist.all_gather_object(uuids, uuid)
+
+    # the load window around the timed region: about 0.4 s of untimed replays
+    # before it and 0.2 s after it, the same count on every rank (rank 0's)
+    e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_a.record()
+    for _ in range(5):
+        graph.replay()
+    e_b.record()
+    torch.cuda.synchronize()
+    est_ms = max(e_a.elapsed_time(e_b) / 5, 1e-3)
+    n_window = torch.tensor([min(20000, int(400.0 / est_ms) + 1)], device=dev)
+    if world > 1:
+        dist.broadcast(n_window, src=0)
+    n_pre = int(n_window.item())
+    n_post = max(1, n_pre // 2)
 
     # ---- timed region: K steps (graph replays), CUDA events, max over ranks
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(uuid)
+    sampler = ClockSampler(uuids, active=rank == 0)
     with sampler:
-        time.sleep(0.3)
         barrier()
         torch.cuda.synchronize()
+        sampler.mark()
+        for _ in range(n_pre):
+            graph.replay()
         start.record()
         for _ in range(args.steps):
             graph.replay()
         end.record()
+        for _ in range(n_post):
+            graph.replay()
         torch.cuda.synchronize()
+        sampler.mark()
         barrier()
     ms = start.elapsed_time(end) / args.steps
     if world > 1:
@@ -605,30 +749,44 @@ def run_ours(args):
     for t, h in zip(e2e_in, hosts_in):
         h.copy_(t.cpu())
     hosts_out = [torch.empty_like(t, device="cpu").pin_memory() for t in e2e_out]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for it in range(3 + args.e2e_steps):
-        if it == 3:
-            barrier()
-            torch.cuda.synchronize()
-            e0.record()
-        for t, h in zip(e2e_in, hosts_in):
-            t.copy_(h, non_blocking=True)
-        step()
-        for t, h in zip(e2e_out, hosts_out):
-            h.copy_(t, non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    def e2e_ms_of(run_step):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for it in range(3 + args.e2e_steps):
+            if it == 3:
+                barrier()
+                torch.cuda.synchronize()
+                e0.record()
+            for t, h in zip(e2e_in, hosts_in):
+                t.copy_(h, non_blocking=True)
+            run_step()
+            for t, h in zip(e2e_out, hosts_out):
+                h.copy_(t, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        ms_ = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([ms_], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_ = float(t.item())
+        return ms_
+
+    eager_ms = e2e_ms_of(step)
+    e2e_ms = e2e_ms_of(prepared.run) if prepared is not None else eager_ms
     e2e = {"value": round(STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
            "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_in),
            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_out),
            "ms_per_step": round(e2e_ms, 4),
-           "path": ("fp8gq.dist.PeerGather paired linears (eager)" if paired else
-                    "fp8gq.fused_gemv_quant (eager) per linear")}
+           "path": (("fp8gq.LaunchList of prepared " + ("PeerGather paired linears" if paired else
+                                                          "PeerGather.prepare_linear calls" if pg is not None else
+                                                          "fp8gq.prepare_fused_gemv_quant calls") +
+                     ", one run per step (eager, no graph)") if prepared is not None else
+                    "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
+           "prepared_matches_calls": prepared_same,
+           "eager_calls": {"ms_per_step": round(eager_ms, 4),
+                           "value": round(STEP_BYTES / (eager_ms * 1e-3) / 1e9, 3),
+                           "path": ("fp8gq.dist.PeerGather paired linears (eager)" if paired else
+                                    "fp8gq.dist.PeerGather.linear (eager)" if pg is not None else
+                                    "fp8gq.fused_gemv_quant (eager) per linear")}}
 
     torch.cuda.synchronize()
     assert fp8gq.device_error() == 0, "a kernel recorded a wait timeout"
@@ -661,7 +819,7 @@ def run_ours(args):
                            "static_weights": bool(args.static_weights)},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
                 "per_linear": per, "per_linear_row_kernel": per_row, "per_linear_tile_kernel": per_tm, **extra,
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "parity": parity,
                 "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:

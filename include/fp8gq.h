@@ -302,6 +302,20 @@ int fp8gq_set_tm_options(int flags);
  * no error was recorded. */
 int fp8gq_device_error(uint32_t *code, int clear);
 
+/* Sets the current device's limit of the bounded waits in the kernels, in
+ * nanoseconds, 1 ms .. 20 s (default 2 s): a gathered call's wait for the
+ * peers' flags gives up after it, a wait for work inside the same kernel (a
+ * ring, accumulator or split-K wait) after twice it, so that a lost peer is
+ * reported by the peer wait.  *previous (may be NULL) receives the old
+ * limit.  Synchronous.  A wait
+ * that runs out records its site in the device error word and the kernel
+ * finishes without hanging -- this is the failure path that replaces the
+ * reference's catch-all fallback (patches/patch_fp8_fused_tail.py:16-26):
+ * a lost peer or a stuck copy becomes FP8GQ_ERR_DEVICE_TIMEOUT on the host.
+ * Lowering the limit lets a test make a wait run out on purpose; leave the
+ * default in production.  FP8GQ_ERR_UNSUPPORTED for a limit out of range. */
+int fp8gq_set_wait_limit_ns(uint64_t limit_ns, uint64_t *previous);
+
 /* Stack runner: a list of block-FP8 linears -- e.g. the qkv, o, gate_up and
  * down (SwiGLU) linears of every layer of a decode step -- run in list order
  * by ONE persistent, cooperative launch on all SMs.  Each linear is the tile
@@ -365,6 +379,56 @@ int fp8gq_stack_prepare(const fp8gq_stack_linear *lin, int n, int M, void *devic
  * and the plan must be prepared again. */
 int fp8gq_stack_run(const fp8gq_stack_plan *plan, fp8gq_stream_t stream);
 
+/* Prepared launches.  A decode loop calls the same linears on the same
+ * buffers every step; most of a call's host time is spent on work that does
+ * not change between steps -- argument checks, routing, tensor-map encoding,
+ * grid choice, the kernel parameter block.  fp8gq_prepare_<entry point> takes
+ * the arguments of <entry point> (without the stream), does all of that once
+ * and stores the resulting kernel launches (one to three) in *plan, launching
+ * nothing; fp8gq_launch_plans then issues the launches of n plans, in array
+ * order, on `stream`, with no other host work.  The result of launching a plan
+ * is the result of the entry point it was prepared from: same kernels, same
+ * parameters.  A plan holds raw device pointers (operands, outputs, workspace,
+ * peer buffers) and the process-wide switches in force when it was prepared
+ * (fp8gq_set_static_weights, fp8gq_set_tm_options): prepare it again after any
+ * of them changes.  Plans are plain data: they may be copied byte for byte,
+ * e.g. into one array for fp8gq_launch_plans, and are launched on the device
+ * that was current when they were prepared (FP8GQ_ERR_DEVICE otherwise).
+ * Launches of plans that share a workspace or a gather descriptor's counters
+ * must not overlap on the GPU.  fp8gq_launch_plans stops at the first plan that
+ * fails and returns its status.  No counterpart in the reference (which pays
+ * Triton's launch path on every call, and removes it with CUDA graphs). */
+#define FP8GQ_LAUNCH_PLAN_BYTES 4096
+typedef struct fp8gq_launch_plan {
+    uint64_t opaque[FP8GQ_LAUNCH_PLAN_BYTES / 8];
+} fp8gq_launch_plan;
+
+int fp8gq_prepare_fused_gemv_quant(const void *x, int64_t ldx, const void *w, int64_t ldw,
+                                   const float *ws, int64_t ldws, void *out, int64_t ldo,
+                                   int M, int N, int K, uint8_t *xq_out, float *sx_out,
+                                   void *workspace, size_t workspace_bytes, fp8gq_launch_plan *plan);
+int fp8gq_prepare_fused_swiglu_q_gemm(const void *gu, int64_t ldgu, const void *w, int64_t ldw,
+                                      const float *ws, int64_t ldws, void *out, int64_t ldo,
+                                      int M, int N, int I, uint8_t *xq_out, float *sx_out,
+                                      void *workspace, size_t workspace_bytes, fp8gq_launch_plan *plan);
+int fp8gq_prepare_fused_gemv_quant_gather(const void *x, int64_t ldx, const void *w, int64_t ldw,
+                                          const float *ws, int64_t ldws, int M, int N, int K,
+                                          const fp8gq_gather *gather, void *workspace, size_t workspace_bytes,
+                                          fp8gq_launch_plan *plan);
+int fp8gq_prepare_fused_swiglu_q_gemm_gather(const void *gu, int64_t ldgu, const void *w, int64_t ldw,
+                                             const float *ws, int64_t ldws, int M, int N, int I,
+                                             const fp8gq_gather *gather, void *workspace,
+                                             size_t workspace_bytes, fp8gq_launch_plan *plan);
+int fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant(const void *x, int nsrc, int64_t src_stride, int64_t ldx,
+                                                      const void *residual, int64_t ldr, const void *norm_w,
+                                                      float eps, const void *w, int64_t ldw, const float *ws,
+                                                      int64_t ldws, void *out, int64_t ldo, void *residual_out,
+                                                      int64_t ldro, int M, int N, int K, uint8_t *xq_out,
+                                                      float *sx_out, const fp8gq_gather *wait, void *workspace,
+                                                      size_t workspace_bytes, fp8gq_launch_plan *plan);
+int fp8gq_prepare_gather_wait(const fp8gq_gather *gather, fp8gq_launch_plan *plan);
+int fp8gq_launch_plans(const fp8gq_launch_plan *plans, int n, fp8gq_stream_t stream);
+
 /* fp8gq_gemv_quant_tm without a workspace argument.  No counterpart in the
  * reference (its Triton kernels need no scratch).
  *
@@ -382,8 +446,9 @@ int fp8gq_stack_run(const fp8gq_stack_plan *plan, fp8gq_stream_t stream);
  * M <= 16 with N <= 524288 and K <= 131072 fits.
  *
  * The first call on a device looks up the array's device address (once per
- * device, with that device current); make that first call before any stream
- * capture begins.  Every call clears the array's split-K counters with an
+ * device, with that device current) and keeps it for the life of the
+ * process; make that first call before any stream capture begins, and do not
+ * reset the device (cudaDeviceReset) between calls.  Every call clears the array's split-K counters with an
  * asynchronous memset on `stream` and then reuses the array, which keeps the
  * last call's partial sums: calls whose kernels overlap on the GPU (two
  * streams, two host threads) race on it, so issue them on one stream.

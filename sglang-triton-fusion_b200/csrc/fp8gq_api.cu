@@ -25,6 +25,8 @@ using namespace fp8gq;
 namespace {
 
 constexpr int kMaxDevices = 64;
+constexpr uint64_t kMinWaitLimitNs = 1000000ull;        // 1 ms
+constexpr uint64_t kMaxWaitLimitNs = 20000000000ull;    // 20 s
 
 struct DeviceInfo {
   int sm_count = 0;
@@ -591,6 +593,16 @@ int fp8gq_set_tm_options(int flags) {
   return g_tm_options.exchange(flags);
 }
 
+int fp8gq_set_wait_limit_ns(uint64_t limit_ns, uint64_t* previous) {
+  if (limit_ns < kMinWaitLimitNs || limit_ns > kMaxWaitLimitNs) return FP8GQ_ERR_UNSUPPORTED;
+  unsigned long long old = 0;
+  if (cudaMemcpyFromSymbol(&old, g_wait_limit_ns, sizeof(old)) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  const unsigned long long v = limit_ns;
+  if (cudaMemcpyToSymbol(g_wait_limit_ns, &v, sizeof(v)) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  if (previous) *previous = old;
+  return FP8GQ_OK;
+}
+
 int fp8gq_device_error(uint32_t* code, int clear) {
   if (!code) return FP8GQ_ERR_NULL_POINTER;
   unsigned int v = 0;
@@ -832,7 +844,9 @@ void* g_noalloc_addr[kMaxDevices] = {};
 
 // Device address of g_noalloc_scratch on the current device.  In host code
 // the array's name is only a host-side stand-in, so the address is looked up
-// once per device with that device current, and cached.
+// once per device with that device current, and kept for the life of the
+// process (a cudaDeviceReset between calls would leave it stale; the entry
+// point's documentation says not to do that).
 int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return FP8GQ_ERR_DEVICE;
@@ -871,3 +885,108 @@ extern "C" int fp8gq_gemv_quant_tm_noalloc(const void* x, int64_t ldx, const voi
                    g_static_weights.load(std::memory_order_relaxed), 0, tm_resident_mode(),
                    tm_cluster_mode());
 }
+
+// ---------------------------------------------------------------------------
+// Prepared launches: the entry points above, recorded once and issued later
+// (fp8gq_prepare_* / fp8gq_launch_plans in include/fp8gq.h).
+// ---------------------------------------------------------------------------
+namespace {
+
+static_assert(sizeof(LaunchRecord) <= sizeof(fp8gq_launch_plan), "fp8gq_launch_plan too small for a record");
+static_assert(alignof(LaunchRecord) <= alignof(fp8gq_launch_plan), "fp8gq_launch_plan under-aligned");
+
+// Runs `issue` (an entry point called with a null stream) with a recorder
+// installed, so that its launches land in `plan` instead of a stream.
+template <typename F>
+int prepare_into(fp8gq_launch_plan* plan, F&& issue) {
+  if (!plan) return FP8GQ_ERR_NULL_POINTER;
+  LaunchRecord* rec = reinterpret_cast<LaunchRecord*>(plan);
+  std::memset(rec, 0, sizeof(*rec));
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FP8GQ_ERR_DEVICE;
+  rec->device = dev;
+  int st;
+  {
+    RecordScope scope(rec);
+    st = issue();
+  }
+  if (st == FP8GQ_OK && (rec->overflow || rec->n == 0)) st = FP8GQ_ERR_UNSUPPORTED;
+  rec->magic = st == FP8GQ_OK ? kRecMagic : 0;
+  return st;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fp8gq_prepare_fused_gemv_quant(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
+                                   int64_t ldws, void* out, int64_t ldo, int M, int N, int K, uint8_t* xq_out,
+                                   float* sx_out, void* workspace, size_t workspace_bytes, fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] {
+    return fp8gq_fused_gemv_quant(x, ldx, w, ldw, ws, ldws, out, ldo, M, N, K, xq_out, sx_out, workspace,
+                                  workspace_bytes, nullptr);
+  });
+}
+
+int fp8gq_prepare_fused_swiglu_q_gemm(const void* gu, int64_t ldgu, const void* w, int64_t ldw, const float* ws,
+                                      int64_t ldws, void* out, int64_t ldo, int M, int N, int I, uint8_t* xq_out,
+                                      float* sx_out, void* workspace, size_t workspace_bytes,
+                                      fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] {
+    return fp8gq_fused_swiglu_q_gemm(gu, ldgu, w, ldw, ws, ldws, out, ldo, M, N, I, xq_out, sx_out, workspace,
+                                     workspace_bytes, nullptr);
+  });
+}
+
+int fp8gq_prepare_fused_gemv_quant_gather(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* ws,
+                                          int64_t ldws, int M, int N, int K, const fp8gq_gather* gather,
+                                          void* workspace, size_t workspace_bytes, fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] {
+    return fp8gq_fused_gemv_quant_gather(x, ldx, w, ldw, ws, ldws, M, N, K, gather, workspace, workspace_bytes,
+                                         nullptr);
+  });
+}
+
+int fp8gq_prepare_fused_swiglu_q_gemm_gather(const void* gu, int64_t ldgu, const void* w, int64_t ldw,
+                                             const float* ws, int64_t ldws, int M, int N, int I,
+                                             const fp8gq_gather* gather, void* workspace, size_t workspace_bytes,
+                                             fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] {
+    return fp8gq_fused_swiglu_q_gemm_gather(gu, ldgu, w, ldw, ws, ldws, M, N, I, gather, workspace,
+                                            workspace_bytes, nullptr);
+  });
+}
+
+int fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant(
+    const void* x, int nsrc, int64_t src_stride, int64_t ldx, const void* residual, int64_t ldr, const void* norm_w,
+    float eps, const void* w, int64_t ldw, const float* ws, int64_t ldws, void* out, int64_t ldo, void* residual_out,
+    int64_t ldro, int M, int N, int K, uint8_t* xq_out, float* sx_out, const fp8gq_gather* wait, void* workspace,
+    size_t workspace_bytes, fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] {
+    return fp8gq_fused_reduce_add_rmsnorm_gemv_quant(x, nsrc, src_stride, ldx, residual, ldr, norm_w, eps, w, ldw,
+                                                     ws, ldws, out, ldo, residual_out, ldro, M, N, K, xq_out, sx_out,
+                                                     wait, workspace, workspace_bytes, nullptr);
+  });
+}
+
+int fp8gq_prepare_gather_wait(const fp8gq_gather* gather, fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] { return fp8gq_gather_wait(gather, nullptr); });
+}
+
+int fp8gq_launch_plans(const fp8gq_launch_plan* plans, int n, fp8gq_stream_t stream) {
+  if (n < 0) return FP8GQ_ERR_SHAPE;
+  if (n > 0 && !plans) return FP8GQ_ERR_NULL_POINTER;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FP8GQ_ERR_DEVICE;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  for (int i = 0; i < n; ++i) {
+    const LaunchRecord* rec = reinterpret_cast<const LaunchRecord*>(plans + i);
+    if (rec->magic != kRecMagic || rec->n < 1 || rec->n > kRecMaxLaunches) return FP8GQ_ERR_UNSUPPORTED;
+    if (rec->device != dev) return FP8GQ_ERR_DEVICE;
+    const cudaError_t e = launch_recorded(*rec, s);
+    if (e != cudaSuccess) return cuda_fail(e, "fp8gq_launch_plans");
+  }
+  return FP8GQ_OK;
+}
+
+}  // extern "C"

@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
+#include <type_traits>
 #include <utility>
 
 namespace fp8gq {
@@ -48,9 +50,22 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Give up after ~2 s: every wait in these kernels is for work of the same CTA
-// (or the same grid) that completes in microseconds.
+// Every wait in these kernels is for work that completes in microseconds: of
+// the same CTA or grid, or a peer GPU's kernel of the same step.  A wait for
+// the peers' flags gives up after the peer limit (2 s by default); a wait for
+// work inside the same kernel after twice that, so that when a peer is lost
+// the peer wait is the one that gives up and reports it, and the waits queued
+// behind it complete once it has.  The limit is a device variable so that a
+// test can shorten it (fp8gq_set_wait_limit_ns) and make a wait run out on
+// purpose; it is read only on the slow path of a wait, after its first polls
+// failed.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+__device__ unsigned long long g_wait_limit_ns = kWaitLimitNs;
+
+__device__ __forceinline__ uint64_t peer_wait_limit_ns() {
+  return *reinterpret_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
+__device__ __forceinline__ uint64_t wait_limit_ns() { return 2 * peer_wait_limit_ns(); }
 
 // ---------------------------------------------------------------------------
 // mbarrier + 1-D bulk copy (TMA, no tensor map, no multicast)
@@ -94,13 +109,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity to complete; false (and the error
-// word set) if that takes longer than kWaitLimitNs.
+// word set) if that takes longer than the wait limit (wait_limit_ns).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int site) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && global_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 0u && global_ns() - t0 > wait_limit_ns()) {
       record_error(site);
       return false;
     }
@@ -351,6 +366,15 @@ constexpr int kMaxGatherRanks = 8;
 // gathered output has landed here.  All ranks run the same sequence of
 // gathered kernels, so their sequence numbers advance together.
 //
+// Stores into a peer never overtake that peer: a publishing kernel stores
+// into the ranks' buffers only once every rank's flag has reached this rank's
+// sequence number, i.e. once every rank has finished its previous publishing
+// kernel (with wait_input that is the input wait itself; without it the
+// storing warps wait the same way before their first store).  So everything a
+// rank queued before its previous publishing call -- readers of the buffer
+// about to be overwritten included -- is complete before any rank writes into
+// its buffers again.
+//
 // A K-sharded (row-parallel) linear uses the same stores for its partial
 // output: out[r] points at this rank's slab in rank r's buffer of per-rank
 // partials, col0 = 0.  A kernel with local_out set only waits (wait_input) and
@@ -417,7 +441,7 @@ __device__ __forceinline__ bool gather_wait_input(const GatherParams& g, int lan
     const uint64_t t0 = global_ns();
     for (uint32_t it = 0;; ++it) {
       if (static_cast<int>(ld_acquire_sys_u32(flag) - s) >= 0) break;
-      if ((it & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+      if ((it & 255u) == 255u && global_ns() - t0 > peer_wait_limit_ns()) {
         record_error(kSiteGather);
         ok = false;
         break;
@@ -427,18 +451,111 @@ __device__ __forceinline__ bool gather_wait_input(const GatherParams& g, int lan
   return __all_sync(0xffffffffu, ok) != 0;
 }
 
-// Host: launch with programmatic stream serialization (the kernel pairs it with
-// grid_dependency_wait / grid_launch_dependents) and, for cluster_x > 1,
-// thread-block clusters of cluster_x consecutive CTAs.
+// One warp (all 32 lanes), before its first store of a publishing kernel's
+// output: the stores may not overtake a rank still inside its previous
+// publishing kernel.  A kernel with wait_input has made that wait already; for
+// any other publishing kernel this is the same bounded wait.
+__device__ __forceinline__ void gather_wait_store(const GatherParams& g, int lane) {
+  if (gather_publishes(g) && !g.wait_input) gather_wait_input(g, lane);
+}
+
+// ---------------------------------------------------------------------------
+// Host: recorded launches.  A decode loop calls the same linears on the same
+// buffers every step, so the per-call host work -- argument checks, routing,
+// tensor-map encoding, grid choice, the parameter block -- can be done once.
+// While a LaunchRecord is installed on the calling host thread (RecordScope),
+// launch_with_pdl_cluster stores each launch (kernel, grid, block, shared
+// memory, cluster size and the parameter bytes) instead of issuing it;
+// launch_recorded issues them later on any stream.  A record is plain data,
+// valid at any address (the runtime copies each parameter from the pointer it
+// is given), so callers may copy it.
+// ---------------------------------------------------------------------------
+constexpr int kRecMaxLaunches = 3;    // group quant + up to two tile-kernel passes
+constexpr int kRecMaxArgs = 12;
+constexpr int kRecArgBytes = 1024;
+
+struct RecordedLaunch {
+  const void* fn;
+  dim3 grid, block;
+  size_t smem;
+  int cluster_x;
+  int nargs;
+  uint16_t arg_off[kRecMaxArgs];
+  uint16_t arg_size[kRecMaxArgs];
+  unsigned char args[kRecArgBytes];
+};
+
+struct LaunchRecord {
+  uint64_t magic;
+  int device;
+  int n;
+  int overflow;
+  int reserved;
+  RecordedLaunch launch[kRecMaxLaunches];
+};
+constexpr uint64_t kRecMagic = 0x66703867714c5031ull;   // "fp8gqLP1"
+
+inline LaunchRecord*& current_recorder() {
+  static thread_local LaunchRecord* rec = nullptr;
+  return rec;
+}
+
+// Installs `rec` as this thread's recorder for the scope's lifetime.
+struct RecordScope {
+  LaunchRecord* prev;
+  explicit RecordScope(LaunchRecord* rec) : prev(current_recorder()) { current_recorder() = rec; }
+  ~RecordScope() { current_recorder() = prev; }
+  RecordScope(const RecordScope&) = delete;
+  RecordScope& operator=(const RecordScope&) = delete;
+};
+
 template <typename... KArgs, typename... Args>
-inline cudaError_t launch_with_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
-                                           cudaStream_t stream, int cluster_x, Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
+inline cudaError_t record_launch(LaunchRecord* rec, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 int cluster_x, Args&&... args) {
+  static_assert(sizeof...(KArgs) == sizeof...(Args), "one value per kernel parameter");
+  static_assert(sizeof...(KArgs) <= kRecMaxArgs, "too many kernel parameters to record");
+  if (rec->n >= kRecMaxLaunches) {
+    rec->overflow = 1;
+    return cudaErrorInvalidValue;
+  }
+  RecordedLaunch& L = rec->launch[rec->n];
+  L.fn = reinterpret_cast<const void*>(kernel);
+  L.grid = grid;
+  L.block = block;
+  L.smem = smem;
+  L.cluster_x = cluster_x;
+  L.nargs = 0;
+  size_t off = 0;
+  bool fits = true;
+  auto put = [&](const auto& v) {
+    using T = std::decay_t<decltype(v)>;
+    off = (off + alignof(T) - 1) / alignof(T) * alignof(T);
+    if (off + sizeof(T) > static_cast<size_t>(kRecArgBytes)) {
+      fits = false;
+      return;
+    }
+    std::memcpy(L.args + off, &v, sizeof(T));
+    L.arg_off[L.nargs] = static_cast<uint16_t>(off);
+    L.arg_size[L.nargs] = static_cast<uint16_t>(sizeof(T));
+    ++L.nargs;
+    off += sizeof(T);
+  };
+  (put(static_cast<std::decay_t<KArgs>>(std::forward<Args>(args))), ...);
+  if (!fits) {
+    rec->overflow = 1;
+    return cudaErrorInvalidValue;
+  }
+  ++rec->n;
+  return cudaSuccess;
+}
+
+inline void pdl_config(cudaLaunchConfig_t& cfg, cudaLaunchAttribute (&attr)[2], dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, int cluster_x) {
+  cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
@@ -450,6 +567,35 @@ inline cudaError_t launch_with_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, 
     attr[1].val.clusterDim.z = 1;
     cfg.numAttrs = 2;
   }
+}
+
+// Issues a record's launches on `stream`, in order.
+inline cudaError_t launch_recorded(const LaunchRecord& rec, cudaStream_t stream) {
+  for (int i = 0; i < rec.n; ++i) {
+    const RecordedLaunch& L = rec.launch[i];
+    void* argv[kRecMaxArgs];
+    for (int a = 0; a < L.nargs; ++a) argv[a] = const_cast<unsigned char*>(L.args) + L.arg_off[a];
+    cudaLaunchConfig_t cfg;
+    cudaLaunchAttribute attr[2];
+    pdl_config(cfg, attr, L.grid, L.block, L.smem, stream, L.cluster_x);
+    const cudaError_t e = cudaLaunchKernelExC(&cfg, L.fn, argv);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Host: launch with programmatic stream serialization (the kernel pairs it with
+// grid_dependency_wait / grid_launch_dependents) and, for cluster_x > 1,
+// thread-block clusters of cluster_x consecutive CTAs -- or, with a recorder
+// installed on this thread, record the launch.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_with_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                           cudaStream_t stream, int cluster_x, Args&&... args) {
+  if (LaunchRecord* rec = current_recorder())
+    return record_launch(rec, kernel, grid, block, smem, cluster_x, std::forward<Args>(args)...);
+  cudaLaunchConfig_t cfg;
+  cudaLaunchAttribute attr[2];
+  pdl_config(cfg, attr, grid, block, smem, stream, cluster_x);
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -256,7 +256,7 @@ __device__ __forceinline__ bool tag_wait(volatile uint32_t* tag, uint32_t want) 
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (*tag == want) return true;
-    if ((it & 255u) == 0u && global_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 0u && global_ns() - t0 > wait_limit_ns()) {
       record_error(kSiteTmAcc);
       return false;
     }
@@ -874,6 +874,9 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   } else {
     // -------------------------------------------------------- epilogue --
+    // (publishing without an input wait: no store may overtake a rank still
+    // inside its previous publishing kernel; the MMA pipeline runs meanwhile)
+    gather_wait_store(p.gather, lane);
     const int q4 = warp & 3;                 // TMEM lane quarter of this warp
     const int row = 32 * q4 + lane;          // weight row within the 128-row block
     const uint32_t t_lane = static_cast<uint32_t>(32 * q4) << 16;

@@ -317,6 +317,7 @@ gemv_row_kernel(const RowParams p) {
   int nb_cur = -1;
   bool ok = true;
   int win_buf = 0;
+  bool store_wait = true;   // publishing: warp 0 waits for the ranks before its first store
   const int my_row_in_group = row_of_lane<R>(lane);
   const bool row_writer = (lane & ((32 / R) - 1)) == 0;
 
@@ -359,6 +360,10 @@ gemv_row_kernel(const RowParams p) {
     if (done_rows % kRowWindow == 0 || j == n_my - 1) {
       named_bar_sync(1, T);
       if (warp == 0) {
+        if (store_wait) {
+          gather_wait_store(p.gather, lane);
+          store_wait = false;
+        }
         const int wrow0 = ((done_rows - 1) / kRowWindow) * kRowWindow;
         const int nrows = done_rows - wrow0;
         if (lane < nrows) {

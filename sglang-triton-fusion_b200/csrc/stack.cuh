@@ -94,7 +94,7 @@ struct StackParams {
 constexpr size_t kStTailBytes = (3 * kStMaxStages + 2 * kTmMaxAcc + 1) * 8 + 16 + kStRing * 4 + kStRing * 4 +
                                 kStRing * kStMT * 4;
 
-// Bounded wait helpers: give up after kWaitLimitNs, or at once when another
+// Bounded wait helpers: give up after the wait limit, or at once when another
 // CTA (or an earlier launch) has recorded a device error.
 __device__ __forceinline__ bool st_error_seen() {
   return *reinterpret_cast<volatile unsigned int*>(&g_device_error) != 0u;
@@ -107,7 +107,7 @@ __device__ __forceinline__ bool st_mbar_wait(uint64_t* bar, uint32_t parity, uns
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0u) {
       if (st_error_seen()) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > wait_limit_ns()) {
         record_error(site);
         return false;
       }
@@ -129,7 +129,7 @@ __device__ __forceinline__ bool st_wait_count(const unsigned int* p, unsigned in
     if (ld_acquire_gpu_u32(p) >= want) return true;
     if ((it & 63u) == 0u) {
       if (st_error_seen()) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > wait_limit_ns()) {
         record_error(kSiteStackDep);
         return false;
       }
@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(kStThreads, 1) stack_kernel(const StackParams 
             if (*tag != want) {
               const uint64_t t0 = global_ns();
               for (uint32_t it = 1; *tag != want; ++it)
-                if ((it & 255u) == 0u && (st_error_seen() || global_ns() - t0 > kWaitLimitNs)) {
+                if ((it & 255u) == 0u && (st_error_seen() || global_ns() - t0 > wait_limit_ns())) {
                   record_error(kSiteStackRing);
                   ok = false;
                   break;

@@ -44,6 +44,11 @@ class Gather(ctypes.Structure):
                 ("local_out", ctypes.c_int)]
 
 
+class LaunchPlan(ctypes.Structure):
+    """struct fp8gq_launch_plan (include/fp8gq.h): opaque, copyable bytes."""
+    _fields_ = [("opaque", ctypes.c_uint64 * 512)]
+
+
 class StackLinear(ctypes.Structure):
     """struct fp8gq_stack_linear (include/fp8gq.h)."""
     _fields_ = [("x", ctypes.c_void_p), ("ldx", ctypes.c_int64),
@@ -79,6 +84,7 @@ SIGNATURES = {
     "fp8gq_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_swiglu_group_quant": (_I, [_P, _I64, _I, _I, _P, _P, _P]),
     "fp8gq_device_error": (_I, [ctypes.POINTER(ctypes.c_uint32), _I]),
+    "fp8gq_set_wait_limit_ns": (_I, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64)]),
     "fp8gq_add_rmsnorm": (_I, [_P, _I64, _P, _I64, _P, ctypes.c_float, _P, _I64, _P, _I64, _I, _I, _P]),
     "fp8gq_fused_add_rmsnorm_gemv_quant": (_I, [_P, _I64, _P, _I64, _P, ctypes.c_float, _P, _I64, _P, _I64,
                                                 _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ, _P]),
@@ -102,6 +108,20 @@ SIGNATURES = {
     "fp8gq_stack_prepare": (_I, [ctypes.POINTER(StackLinear), _I, _I, _P, _SZ, ctypes.POINTER(StackPlan), _P]),
     "fp8gq_stack_run": (_I, [ctypes.POINTER(StackPlan), _P]),
     "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),
+    "fp8gq_prepare_fused_gemv_quant": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ,
+                                            ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_prepare_fused_swiglu_q_gemm": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ,
+                                               ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_prepare_fused_gemv_quant_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
+                                                   _P, _SZ, ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_prepare_fused_swiglu_q_gemm_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I,
+                                                      ctypes.POINTER(Gather), _P, _SZ, ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, ctypes.c_float, _P,
+                                                               _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P,
+                                                               ctypes.POINTER(Gather), _P, _SZ,
+                                                               ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_prepare_gather_wait": (_I, [ctypes.POINTER(Gather), ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_launch_plans": (_I, [ctypes.POINTER(LaunchPlan), _I, _P]),
 }
 
 
@@ -183,3 +203,15 @@ def device_error(clear: bool = False) -> int:
     code = ctypes.c_uint32(0)
     check(lib.fp8gq_device_error(ctypes.byref(code), 1 if clear else 0), "fp8gq_device_error")
     return int(code.value)
+
+
+SITE_GATHER = 8   # kSiteGather: the wait for the peers' flags of a gathered call
+
+
+def set_wait_limit_ns(limit_ns: int) -> int:
+    """Limit of every bounded wait on the current device, in nanoseconds
+    (1 ms .. 20 s; default 2 s); returns the previous limit.  Lower it only to
+    make a wait run out on purpose in a test (fp8gq_set_wait_limit_ns)."""
+    prev = ctypes.c_uint64(0)
+    check(load().fp8gq_set_wait_limit_ns(int(limit_ns), ctypes.byref(prev)), "fp8gq_set_wait_limit_ns")
+    return int(prev.value)

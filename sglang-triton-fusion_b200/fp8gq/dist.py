@@ -249,6 +249,81 @@ class PeerGather:
         return ops.fused_reduce_add_rmsnorm_gemv_quant(slabs, residual, norm_weight, Wq_rows, Ws_rows, eps,
                                                        out=out, residual_out=residual_out, wait=g)
 
+    # ---- prepared launches (fp8gq.prepared): the same calls, recorded once
+    def prepare_linear(self, x: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Tensor, out: torch.Tensor,
+                       wait_input: bool = True, desc=None):
+        """The plan of ``linear(x, Wq_shard, Ws_shard, out, wait_input)``."""
+        from .prepared import Plan
+        M, K = x.shape
+        Nr, ldw, ldws = ops._check_weight_strides(Wq_shard, Ws_shard, K)
+        if out.shape != (M, Nr * self.world):
+            raise ops.ShapeError(f"out must be [{M}, {Nr * self.world}], got {tuple(out.shape)}")
+        g = desc if desc is not None else self.descriptor(out, self.rank * Nr, wait_input)
+        dev = x.device
+        nbytes = ops._workspace_bytes(self.lib, dev, M, Nr, K)
+        buf, ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, ops._stream(dev)) if nbytes else (None, None, 0)
+        plan = Plan("fp8gq_prepare_fused_gemv_quant_gather", (x, Wq_shard, Ws_shard, out, buf, g), out)
+        st = self.lib.fp8gq_prepare_fused_gemv_quant_gather(
+            x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), ldw, Ws_shard.data_ptr(), ldws, M, Nr, K,
+            ctypes.byref(g), ws_ptr, ws_n, ctypes.byref(plan.cplan))
+        _lib.check(st, plan.what)
+        return plan
+
+    def prepare_linear_partial(self, x: torch.Tensor, Wq_cols: torch.Tensor, Ws_cols: torch.Tensor,
+                               slabs: torch.Tensor, swiglu: bool = False, desc=None):
+        """The plan of ``linear_partial(x, Wq_cols, Ws_cols, slabs, swiglu)``."""
+        from .prepared import Plan
+        M = x.shape[0]
+        N, Kr = Wq_cols.shape
+        if slabs.shape[1:] != (M, N):
+            raise ops.ShapeError(f"slabs must be [{self.world}, {M}, {N}], got {tuple(slabs.shape)}")
+        if x.shape[1] != (2 * Kr if swiglu else Kr):
+            raise ops.ShapeError(f"input must be [M, {2 * Kr if swiglu else Kr}], got {tuple(x.shape)}")
+        _, ldw, ldws = ops._check_weight_strides(Wq_cols, Ws_cols, Kr)
+        g = desc if desc is not None else self.partial_descriptor(slabs)
+        dev = x.device
+        nbytes = ops._workspace_bytes(self.lib, dev, M, N, Kr)
+        buf, ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, ops._stream(dev)) if nbytes else (None, None, 0)
+        name = "fp8gq_prepare_fused_swiglu_q_gemm_gather" if swiglu else "fp8gq_prepare_fused_gemv_quant_gather"
+        plan = Plan(name, (x, Wq_cols, Ws_cols, slabs, buf, g), slabs)
+        st = getattr(self.lib, name)(x.data_ptr(), x.stride(0), Wq_cols.data_ptr(), ldw, Ws_cols.data_ptr(), ldws,
+                                     M, N, Kr, ctypes.byref(g), ws_ptr, ws_n, ctypes.byref(plan.cplan))
+        _lib.check(st, name)
+        return plan
+
+    def prepare_reduce_norm_linear(self, slabs: torch.Tensor, residual: torch.Tensor, norm_weight: torch.Tensor,
+                                   Wq_rows: torch.Tensor, Ws_rows: torch.Tensor, out: torch.Tensor,
+                                   residual_out: torch.Tensor, eps: float = ops.RMS_EPS, desc=None):
+        """The plan of ``reduce_norm_linear(...)``."""
+        from .prepared import Plan
+        if slabs.dim() != 3 or not 1 <= slabs.shape[0] <= _lib.MAX_GATHER_RANKS:
+            raise ops.ShapeError("slabs must be [S, M, K] with 1 <= S <= 8")
+        M, K = ops._check_norm_inputs(slabs[0], residual, norm_weight)
+        N, ldw, ldws = ops._check_weight_strides(Wq_rows, Ws_rows, K)
+        if out.shape != (M, N) or residual_out.shape != (M, K):
+            raise ops.ShapeError("out must be [M, N] and residual_out [M, K]")
+        g = desc if desc is not None else self.wait_descriptor()
+        dev = slabs.device
+        nbytes = ops._workspace_bytes(self.lib, dev, M, N, K)
+        buf, ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, ops._stream(dev)) if nbytes else (None, None, 0)
+        name = "fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant"
+        plan = Plan(name, (slabs, residual, norm_weight, Wq_rows, Ws_rows, out, residual_out, buf, g), out)
+        st = self.lib.fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant(
+            slabs.data_ptr(), slabs.shape[0], slabs.stride(0), slabs.stride(1), residual.data_ptr(), residual.stride(0),
+            norm_weight.data_ptr(), float(eps), Wq_rows.data_ptr(), ldw, Ws_rows.data_ptr(), ldws, out.data_ptr(),
+            out.stride(0), residual_out.data_ptr(), residual_out.stride(0), M, N, K, None, None, ctypes.byref(g),
+            ws_ptr, ws_n, ctypes.byref(plan.cplan))
+        _lib.check(st, name)
+        return plan
+
+    def prepare_wait(self, out: torch.Tensor):
+        """The plan of ``wait(out)``."""
+        from .prepared import Plan
+        g = self.descriptor(out, 0, True)
+        plan = Plan("fp8gq_prepare_gather_wait", (out, g), out)
+        _lib.check(self.lib.fp8gq_prepare_gather_wait(ctypes.byref(g), ctypes.byref(plan.cplan)), plan.what)
+        return plan
+
     def wait(self, out: torch.Tensor):
         """Enqueue a wait for the last gathered call's slices from every rank."""
         g = self.descriptor(out, 0, True)

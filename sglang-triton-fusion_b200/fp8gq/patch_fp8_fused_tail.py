@@ -20,10 +20,14 @@ batches the tile kernel was built for):
 
 * routed -- ``input_scale is None``, bf16 input, e4m3 weight [N, K] with
   N, K multiples of 128, fp32 weight_scale [N/128, K/128], block_size None or
-  [128, 128], CUDA tensors, M = prod(input.shape[:-1]) in [1, 16], K-contiguous
-  operands with 16-byte-aligned rows: M == 1 -> row kernel, 2 <= M <= 16 ->
-  tcgen05 tile kernel.  A routed call never falls back: an error in the
-  fused path raises (the reference swallows exceptions, ``:25-26``).
+  [128, 128], CUDA tensors, M = prod(input.shape[:-1]) in [1, 16]: M == 1 ->
+  row kernel (or the tile kernel for large weights), 2 <= M <= 16 -> tcgen05
+  tile kernel.  The layout never decides the route: an operand the kernels
+  cannot read in place (rows not 16-byte aligned, a non-unit stride along K,
+  a view that does not flatten) is copied into a fresh contiguous buffer
+  first, so a routed call takes the fused path whatever its strides.  A
+  routed call never falls back: an error in the fused path raises (the
+  reference swallows exceptions, ``:25-26``).
 * everything else -- the saved original, called positionally like the
   reference does (``:37-38``, ``:49-50``).
 
@@ -57,7 +61,9 @@ def _on_device(*tensors) -> bool:
 
 
 def route(input, weight, block_size, weight_scale, input_scale) -> str | None:
-    """'row', 'tm' or None (= call the original) for these arguments."""
+    """'row', 'tm' or None (= call the original) for these arguments: the
+    dtypes, shapes and M decide; strides and alignment do not (see
+    fused_linear)."""
     if input_scale is not None or input is None or weight is None or weight_scale is None:
         return None
     if input.dtype != torch.bfloat16 or weight.dtype != torch.float8_e4m3fn:
@@ -67,7 +73,7 @@ def route(input, weight, block_size, weight_scale, input_scale) -> str | None:
     if not _on_device(input, weight, weight_scale):
         return None
     N, K = weight.shape
-    if N % ops.GROUP or K % ops.GROUP or input.shape[-1] != K:
+    if N % ops.GROUP or K % ops.GROUP or input.dim() < 1 or input.shape[-1] != K:
         return None
     if tuple(weight_scale.shape) != (N // ops.GROUP, K // ops.GROUP):
         return None
@@ -76,20 +82,27 @@ def route(input, weight, block_size, weight_scale, input_scale) -> str | None:
     M = input.numel() // K if K else 0
     if M < 1 or M > MAX_FUSED_M:
         return None
-    if weight.stride(1) != 1 or weight_scale.stride(1) != 1 or not _aligned_rows(weight):
-        return None
-    try:
-        x2d = input.view(-1, K)
-    except RuntimeError:
-        return None
-    if x2d.stride(1) != 1 or not _aligned_rows(x2d):
-        return None
     return "row" if M == 1 else "tm"
 
 
+def _readable(t: torch.Tensor, row_align: bool = True) -> torch.Tensor:
+    """t itself when the kernels can read it in place (unit stride along the
+    last dimension, and 16-byte-aligned rows where row_align), else a copy into
+    a fresh contiguous buffer (torch's allocator aligns it to 512 bytes)."""
+    ok = t.stride(-1) == 1 and (not row_align or _aligned_rows(t))
+    return t if ok else t.clone(memory_format=torch.contiguous_format)
+
+
 def fused_linear(input, weight, weight_scale, bias=None) -> torch.Tensor:
-    """The fused path for a routed call (patches/patch_fp8_fused_tail.py:21-24)."""
-    x2d = input.view(-1, input.shape[-1])
+    """The fused path for a routed call (patches/patch_fp8_fused_tail.py:21-24).
+    Operands in a layout the kernels cannot read in place are copied first; a
+    call from sglang never needs that (its activations are contiguous, its
+    weights are parameters), so the copies only keep odd callers on the fused
+    path instead of the original."""
+    K = weight.shape[1]
+    x2d = _readable(input.reshape(-1, K))
+    weight = _readable(weight)
+    weight_scale = _readable(weight_scale, row_align=False)
     out = ops.fused_gemv_quant(x2d, weight, weight_scale)
     if bias is not None:
         out = out + bias

@@ -2,10 +2,10 @@
 own Triton kernels (wafik/sglang-triton-fusion, ``kernels/``) in Triton's CPU
 interpreter (``TRITON_INTERPRET=1``).
 
-Run from the repository root, in a container where the reference checkout is
-at /root/reference:
+Run from the repository root with the path of a reference checkout (or set
+SGLANG_TRITON_FUSION_ROOT to it):
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 The fixtures (``*.npz``) are committed; tests never read the reference.
 
@@ -263,4 +263,7 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SGLANG_TRITON_FUSION_ROOT")
+    if not root:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/reference  (or set SGLANG_TRITON_FUSION_ROOT)")
+    main(root)

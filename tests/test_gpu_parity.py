@@ -565,6 +565,20 @@ def test_patch_wrappers_on_gpu(fp8gq, cuda_device):
             want = fp8gq.fused_gemv_quant(x.view(M, K), wq, ws) + bias
             assert torch.equal(out.view(M, N), want)
         assert not calls
+        # routed sizes whose activation the kernels cannot read in place (rows
+        # starting 8 bytes in; every other element along K) still take the
+        # fused path, through an aligned copy, and match the oracle
+        for M, step in ((1, 1), (4, 1), (3, 2)):
+            x = gpu_activation(M, K, 73 + M, cuda_device)
+            base = torch.zeros(M * K * step + 64, dtype=torch.bfloat16, device=cuda_device)
+            xv = base[4:4 + M * K * step].view(M, K * step)[:, ::step]
+            xv.copy_(x)
+            assert xv.data_ptr() % 16 != 0 or xv.stride(1) != 1
+            out = mod.flashinfer_gemm_w8a8_block_fp8_linear_with_fallback(xv, wq, [128, 128], ws, None, None)
+            assert torch.equal(out, fp8gq.fused_gemv_quant(x, wq, ws))
+            _, exact, _, _ = oracle_of(x, wq, ws)
+            assert_close(to_f32(out), exact, 3.0)
+        assert not calls
         x = gpu_activation(32, K, 72, cuda_device)
         mod.flashinfer_gemm_w8a8_block_fp8_linear_with_fallback(x, wq, [128, 128], ws, None, None)
         assert len(calls) == 1

@@ -83,8 +83,38 @@ def test_route_rejects(fake_sglang):
     assert P.route(x, w, [64, 64], s, None) is None                    # other block size
     assert P.route(x, w, None, s[:1], None) is None                    # scale shape
     assert P.route(x[:, :128], w[:, :128].contiguous(), None, s[:, :1].contiguous(), None) is not None
-    xw = torch.zeros(1, 264, dtype=torch.bfloat16)[:, 4:260]           # rows start 8 bytes in
-    assert P.route(xw, w, None, s, None) is None
+    # layout never decides the route: an activation whose rows start 8 bytes
+    # in, or whose K stride is 2, still goes to the fused path (fused_linear
+    # copies it into an aligned buffer first)
+    xw = torch.zeros(1, 264, dtype=torch.bfloat16)[:, 4:260]
+    assert P.route(xw, w, None, s, None) == "row"
+    assert P.route(torch.zeros(4, 512, dtype=torch.bfloat16)[:, ::2], w, None, s, None) == "tm"
+
+
+@pytest.mark.parametrize("M, stride_k, offset", [(1, 1, 4), (3, 1, 4), (2, 2, 0), (5, 2, 1)])
+def test_unaligned_routed_input_is_copied_not_sent_back(fake_sglang, M, stride_k, offset):
+    mod, calls = fake_sglang
+    P.install(mod)
+    seen = []
+    fused = ops.fused_gemv_quant
+
+    def spy(x2d, Wq, Ws):
+        seen.append((x2d.data_ptr() % 16, x2d.stride(), x2d.is_contiguous()))
+        return fused(x2d, Wq, Ws)
+
+    ops.fused_gemv_quant = spy
+    try:
+        x, w, s = _operands(M)
+        base = torch.zeros(M * 256 * stride_k + 64, dtype=torch.bfloat16)
+        xv = base[offset:offset + M * 256 * stride_k].view(M, 256 * stride_k)[:, ::stride_k]
+        xv.copy_(x)
+        out = mod.cutlass_w8a8_block_fp8_linear_with_fallback(xv, w, [128, 128], s, None, None)
+    finally:
+        ops.fused_gemv_quant = fused
+    assert calls[-1][0] == "fused"
+    assert seen and seen[-1][0] == 0 and seen[-1][1][1] == 1 and (seen[-1][1][0] * 2) % 16 == 0
+    ref, _, _, _ = O.fused_gemv_quant(x.float().numpy(), w.view(torch.uint8).numpy(), s.numpy())
+    assert torch.equal(out, bf16_tensor(ref))
 
 
 def test_routed_call_uses_fused_and_adds_bias(fake_sglang):

@@ -9,6 +9,14 @@ library, so it must agree with the workspace entry point (fp8gq_gemv_quant_tm)
 on every shape that fits, call after call, while the array keeps whatever the
 previous call left in it; shapes that do not fit must be refused.
 
+The array holds the split-K counters and partial sums and, for the
+pre-quantised activation feed, the quantised activation.  The auto choice
+reduces most split-K partial sums inside thread-block clusters, so two cases
+force the other strategies (fp8gq_set_tm_options) to make the array carry the
+data: the split-K hand-off through memory, and the pre-quantised feed.  Each
+alternates two shapes with different row-block counts and splits on one
+stream, so leftover counters and partial sums of one shape meet the next.
+
 The file is named to be collected last; it needs nothing from other tests and
 passes when run on its own in a fresh process.
 """
@@ -74,6 +82,47 @@ def test_noalloc_matches_workspace_entry_point_twice(lib, cuda_device, M, K, N):
         # entry point and against the oracle
         assert_close(to_f32(out), to_f32(ref).astype(np.float64), 3.0)
         assert_close(to_f32(out), exact, 3.0)
+
+
+# two shapes with different row-block counts and splits: (M, K, N)
+ALTERNATING = [(1, 12288, 4096), (4, 4096, 6144)]
+
+
+@pytest.mark.parametrize("option", ["workspace_splitk", "prequant"])
+def test_noalloc_scratch_carries_the_data_across_alternating_shapes(lib, cuda_device, option):
+    import fp8gq
+    flags = {"workspace_splitk": fp8gq.TM_WORKSPACE_SPLITK,
+             "prequant": fp8gq.TM_PREQUANT_ACTIVATIONS | fp8gq.TM_WORKSPACE_SPLITK}[option]
+    ops = [_operands(M, K, N, seed=100 + i, dev=cuda_device) for i, (M, K, N) in enumerate(ALTERNATING)]
+    prev = fp8gq.set_tm_options(flags)
+    try:
+        refs = []
+        for x, wq, ws in ops:
+            ref = torch.empty(x.shape[0], wq.shape[0], dtype=torch.bfloat16, device=cuda_device)
+            assert _call_workspace(lib, x, wq, ws, ref) == 0
+            refs.append(ref)
+        # A, B, A, B, A, B on one stream with no synchronisation in between:
+        # every call starts on the counters and partial sums the last one left
+        outs = []
+        for rep in range(3):
+            for i, (x, wq, ws) in enumerate(ops):
+                out = torch.full((x.shape[0], wq.shape[0]), float("nan"), dtype=torch.bfloat16,
+                                 device=cuda_device)
+                st = _call_noalloc(lib, x, wq, ws, out)
+                assert st == 0, lib.fp8gq_status_string(st)
+                outs.append((i, out))
+        torch.cuda.synchronize()
+    finally:
+        fp8gq.set_tm_options(prev)
+    assert fp8gq.device_error() == 0
+    # same grid, same products, same order of additions: bit-identical to the
+    # workspace entry point under the same options, and within the tile
+    # kernel's tolerance of the oracle
+    for i, out in outs:
+        assert torch.equal(out, refs[i]), f"shape {ALTERNATING[i]}: differs from the workspace entry point"
+    for i, (x, wq, ws) in enumerate(ops):
+        exact = O.fused_gemv_quant(to_f32(x), wq.cpu().view(torch.uint8).numpy(), to_f32(ws))[1]
+        assert_close(to_f32(refs[i]), exact, 3.0)
 
 
 def test_noalloc_refuses_shapes_beyond_its_scratch(lib, cuda_device):
