@@ -749,18 +749,21 @@ def run_ours(args):
     for t, h in zip(e2e_in, hosts_in):
         h.copy_(t.cpu())
     hosts_out = [torch.empty_like(t, device="cpu").pin_memory() for t in e2e_out]
-    def e2e_ms_of(run_step):
+    def e2e_ms_of(run_step, copies=True):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         for it in range(3 + args.e2e_steps):
             if it == 3:
                 barrier()
                 torch.cuda.synchronize()
                 e0.record()
-            for t, h in zip(e2e_in, hosts_in):
-                t.copy_(h, non_blocking=True)
-            run_step()
-            for t, h in zip(e2e_out, hosts_out):
-                h.copy_(t, non_blocking=True)
+            if copies:
+                for t, h in zip(e2e_in, hosts_in):
+                    t.copy_(h, non_blocking=True)
+            if run_step is not None:
+                run_step()
+            if copies:
+                for t, h in zip(e2e_out, hosts_out):
+                    h.copy_(t, non_blocking=True)
         e1.record()
         torch.cuda.synchronize()
         ms_ = e0.elapsed_time(e1) / args.e2e_steps
@@ -772,6 +775,10 @@ def run_ours(args):
 
     eager_ms = e2e_ms_of(step)
     e2e_ms = e2e_ms_of(prepared.run) if prepared is not None else eager_ms
+    # where the end-to-end time goes: the same loop without the copies, and
+    # the copies alone
+    parts_ms = {"without_copies": e2e_ms_of(prepared.run if prepared is not None else step, copies=False),
+                "copies_alone": e2e_ms_of(None)}
     e2e = {"value": round(STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
            "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_in),
            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_out),
@@ -782,6 +789,7 @@ def run_ours(args):
                      ", one run per step (eager, no graph)") if prepared is not None else
                     "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
            "prepared_matches_calls": prepared_same,
+           "parts_ms_per_step": {k: round(v, 4) for k, v in parts_ms.items()},
            "eager_calls": {"ms_per_step": round(eager_ms, 4),
                            "value": round(STEP_BYTES / (eager_ms * 1e-3) / 1e9, 3),
                            "path": ("fp8gq.dist.PeerGather paired linears (eager)" if paired else

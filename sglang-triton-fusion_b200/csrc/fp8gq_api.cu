@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <map>
+#include <tuple>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -126,6 +128,24 @@ constexpr int64_t kRowPreferBytes = 20ll << 20;
 bool m1_uses_row(int N, int K) { return K <= kRowMaxK && static_cast<int64_t>(N) * K <= kRowPreferBytes; }
 constexpr int kRowRingBytes = 96 * 1024;    // per CTA; two CTAs per SM
 
+// Resident CTAs per SM of a row-kernel configuration (occupancy query,
+// cached per kernel, block size and shared memory).
+int row_ctas_per_sm(RowKernel fn, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(fn), threads, smem);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem) != cudaSuccess) n = 0;
+  cudaGetLastError();
+  cache.emplace(key, n);
+  return n;
+}
+
 int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const float* ws, int64_t ldws,
                void* out, int N, int K, uint8_t* xq_out, float* sx_out, cudaStream_t stream,
                const GatherParams* gather = nullptr, const NormParams* norm = nullptr) {
@@ -136,10 +156,6 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   if (K > kRowMaxK) return FP8GQ_ERR_UNSUPPORTED;
   const int n_chunks = K / 16;
   const int c_need = (n_chunks + 383) / 384;
-  int ci = 0;
-  while (kRowCs[ci] < c_need) ++ci;
-  const int C = kRowCs[ci];
-  const int T = ((n_chunks + C - 1) / C + 31) / 32 * 32;
   int ri = 2;
   while (ri > 0 && kRowRs[ri] * K > 16384) --ri;
   const int R = kRowRs[ri];
@@ -147,11 +163,35 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   int stages = kRowRingBytes / stage_bytes;
   if (stages > 16) stages = 16;
   if (stages < 2) stages = 2;
-  const size_t smem = row_smem_bytes(stages, stage_bytes, T / 32);
-  if (smem > static_cast<size_t>(di.max_smem_optin)) return FP8GQ_ERR_UNSUPPORTED;
-
-  RowKernel fn = swiglu ? row_lookup<true>(ci, ri) : row_lookup<false>(ci, ri);
-  if (ensure_max_smem(reinterpret_cast<const void*>(fn), di.max_smem_optin) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+  // Chunks per thread C (and T = the consumer threads that split K): the
+  // fewest that cover K, unless that CTA does not fit twice on an SM (many
+  // threads x many registers, e.g. K = 12288 at C = 2: 416 threads x 85
+  // registers) and a larger C with fewer threads does -- two CTAs per SM
+  // stream faster, and a grid of more CTAs than are resident would run a
+  // second wave.
+  int ci = 0;
+  while (kRowCs[ci] < c_need) ++ci;
+  int T = 0, per_sm = 0;
+  size_t smem = 0;
+  RowKernel fn = nullptr;
+  for (int cj = ci; cj < 6; ++cj) {
+    const int Cj = kRowCs[cj];
+    const int Tj = ((n_chunks + Cj - 1) / Cj + 31) / 32 * 32;
+    const size_t sj = row_smem_bytes(stages, stage_bytes, Tj / 32);
+    if (sj > static_cast<size_t>(di.max_smem_optin)) continue;
+    RowKernel fj = swiglu ? row_lookup<true>(cj, ri) : row_lookup<false>(cj, ri);
+    if (ensure_max_smem(reinterpret_cast<const void*>(fj), di.max_smem_optin) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
+    const int pj = row_ctas_per_sm(fj, Tj + 32, sj);
+    if (pj < 1) continue;
+    if (fn == nullptr || pj > per_sm) {
+      T = Tj;
+      smem = sj;
+      fn = fj;
+      per_sm = pj;
+    }
+    if (pj >= 2) break;
+  }
+  if (fn == nullptr) return FP8GQ_ERR_UNSUPPORTED;
 
   RowParams p;
   p.x = static_cast<const __nv_bfloat16*>(x);
@@ -169,7 +209,8 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   p.gather = gather ? *gather : GatherParams{};
   p.norm = norm ? *norm : NormParams{};
   p.early_weights = g_static_weights.load(std::memory_order_relaxed);
-  int grid = 2 * di.sm_count;
+  // at most two CTAs per SM, and never more than are resident at once
+  int grid = (per_sm < 2 ? per_sm : 2) * di.sm_count;
   if (grid > p.n_groups) grid = p.n_groups;
   if (launch_with_pdl(fn, dim3(grid), dim3(T + 32), smem, stream, p) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
   return launch_status();

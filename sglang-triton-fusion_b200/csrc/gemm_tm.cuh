@@ -492,6 +492,14 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   auto load_ws_cache = [&]() {
     for (int j = tid - 64; j < J; j += kTmThreads - 64) ws_cache[j] = ws_at(j);
   };
+  // resident: the B tiles of the first ring start as zeros (the live rows are
+  // written once the activation is quantised); shared memory only, so this is
+  // done before the grid-dependency wait (barrier 1 below orders it before
+  // those writes)
+  const int nfirst = J < S ? J : S;
+  if (resident && warp >= 2)
+    for (int i = tid - 64; i < nfirst * (Cfg::kBTileBytes / 16); i += kTmThreads - 64)
+      reinterpret_cast<uint4*>(b_tiles)[i] = make_uint4(0u, 0u, 0u, 0u);
   if (early) {
     if (warp >= 2) load_ws_cache();
     if (tid == 0) {
@@ -534,13 +542,10 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     const int jw = tid - 64;
     float ws_first = 0.0f;
     if (!early && jw < J) ws_first = ws_at(jw);
-    // resident: the first ring's B tiles are built here as well (zeros, then
-    // the live rows as they are quantised), so the first MMAs wait only for
-    // their weight tiles
-    const int nfirst = J < S ? J : S;
+    // resident: the first ring's B tiles are built here as well (zeroed before
+    // the wait, the live rows written as they are quantised), so the first
+    // MMAs wait only for their weight tiles
     if (resident) {
-      for (int i = tid - 64; i < nfirst * (Cfg::kBTileBytes / 16); i += kTmThreads - 64)
-        reinterpret_cast<uint4*>(b_tiles)[i] = make_uint4(0u, 0u, 0u, 0u);
       named_bar_sync(1, kTmThreads - 64);
       const int oct = (warp - 2) * 4 + (lane >> 3);
       const int chunk = lane & 7;
@@ -1100,10 +1105,15 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       const int nbc = static_cast<int>(u0 / p.KB);
       const float* part = reinterpret_cast<const float*>(a_tiles);
       for (int e = rank * 128 + (tid - 192); e < p.M * 128; e += 128 * p.csize) {
+        // every rank's value is requested before any is added: one round trip
+        // over distributed shared memory rather than one per rank
+        float v[kTmMaxCluster];
+#pragma unroll
+        for (int q = 0; q < kTmMaxCluster; ++q) v[q] = q < p.csize ? ld_dsmem(dsmem_addr(part + e, q)) : 0.0f;
         float sum = 0.0f;
 #pragma unroll
         for (int q = 0; q < kTmMaxCluster; ++q)
-          if (q < p.csize) sum += ld_dsmem(dsmem_addr(part + e, q));
+          if (q < p.csize) sum += v[q];
         store_out(e >> 7, nbc * 128 + (e & 127), __float2bfloat16_rn(sum));
       }
     }
