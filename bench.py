@@ -773,8 +773,91 @@ def run_ours(args):
             ms_ = float(t.item())
         return ms_
 
+    def e2e_pipelined_ms():
+        """The prepared step with each layer's input copied in on one copy
+        stream and its outputs copied out on another, ordered by events, so
+        the copies of one layer overlap the linears of the others (the same
+        bytes as the serial loop; every copy inside the timed region).  A
+        layer's gathered outputs are complete once the next layer's first
+        linear has waited for them (the last layer's: after the step's final
+        wait), so that is where its copy out starts."""
+        if paired or prepared is None:
+            return None
+        npl = len(SHAPES)
+        per_layer = [fp8gq.LaunchList(prepared.plans[npl * L:npl * (L + 1)]) for L in range(LAYERS)]
+        tail = fp8gq.LaunchList(prepared.plans[npl * LAYERS:]) if len(prepared.plans) > npl * LAYERS else None
+        comp = torch.cuda.current_stream(dev)
+        s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev = lambda: torch.cuda.Event()  # noqa: E731
+        in_ready, in_free = [ev() for _ in range(LAYERS)], [ev() for _ in range(LAYERS)]
+        out_ready, out_free = [ev() for _ in range(LAYERS)], [ev() for _ in range(LAYERS)]
+        h_in, h_out = hosts_in[0], hosts_out[0]
+        done = ev()
+
+        def copy_out(L):
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(out_ready[L])
+                h_out[L].copy_(out_all[L], non_blocking=True)
+                out_free[L].record(s_out)
+
+        def one_step(first):
+            for L in range(LAYERS):
+                with torch.cuda.stream(s_in):
+                    if not first:
+                        s_in.wait_event(in_free[L])          # the last step's linears of layer L have read it
+                    x_all[L].copy_(h_in[L], non_blocking=True)
+                    in_ready[L].record(s_in)
+            for L in range(LAYERS):
+                comp.wait_event(in_ready[L])
+                # out_all[L] is read by the last step's copy out: this rank
+                # rewrites its slice in layer L, and with peer stores the
+                # other ranks rewrite theirs once this rank has finished its
+                # call before layer L (its layer L - 1; for layer 0 the step's
+                # last layer) -- so those layers wait for that copy out too
+                if not first:
+                    comp.wait_event(out_free[L])
+                if world > 1 and L + 1 < LAYERS and not first:
+                    comp.wait_event(out_free[L + 1])
+                if world > 1 and L == LAYERS - 1:
+                    comp.wait_event(out_free[0])             # recorded earlier in this step
+                per_layer[L].run()
+                in_free[L].record(comp)
+                if world == 1:
+                    out_ready[L].record(comp)
+                    copy_out(L)
+                elif L > 0:
+                    out_ready[L - 1].record(comp)            # layer L waited for every slice of layer L - 1
+                    copy_out(L - 1)
+            if tail is not None:
+                tail.run()
+            if world > 1:
+                out_ready[LAYERS - 1].record(comp)
+                copy_out(LAYERS - 1)
+            done.record(s_out)
+
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        one_step(True)
+        for it in range(2 + args.e2e_steps):
+            if it == 2:
+                comp.wait_event(done)
+                torch.cuda.synchronize()
+                barrier()
+                e0.record(comp)
+            one_step(False)
+        comp.wait_event(done)
+        e1.record(comp)
+        torch.cuda.synchronize()
+        ms_ = e0.elapsed_time(e1) / args.e2e_steps
+        if world > 1:
+            t = torch.tensor([ms_], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms_ = float(t.item())
+        return ms_
+
     eager_ms = e2e_ms_of(step)
-    e2e_ms = e2e_ms_of(prepared.run) if prepared is not None else eager_ms
+    serial_ms = e2e_ms_of(prepared.run) if prepared is not None else eager_ms
+    piped_ms = e2e_pipelined_ms()
+    e2e_ms = piped_ms if piped_ms is not None else serial_ms
     # where the end-to-end time goes: the same loop without the copies, and
     # the copies alone
     parts_ms = {"without_copies": e2e_ms_of(prepared.run if prepared is not None else step, copies=False),
@@ -786,8 +869,12 @@ def run_ours(args):
            "path": (("fp8gq.LaunchList of prepared " + ("PeerGather paired linears" if paired else
                                                           "PeerGather.prepare_linear calls" if pg is not None else
                                                           "fp8gq.prepare_fused_gemv_quant calls") +
-                     ", one run per step (eager, no graph)") if prepared is not None else
-                    "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
+                     (", one LaunchList run per layer, each layer's copies in and out on two copy streams "
+                      "overlapping the other layers' linears (eager, no graph)" if piped_ms is not None else
+                      ", one run per step, copies before and after it (eager, no graph)"))
+                    if prepared is not None else "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
+           "serial_copies": {"ms_per_step": round(serial_ms, 4),
+                             "value": round(STEP_BYTES / (serial_ms * 1e-3) / 1e9, 3)},
            "prepared_matches_calls": prepared_same,
            "parts_ms_per_step": {k: round(v, 4) for k, v in parts_ms.items()},
            "eager_calls": {"ms_per_step": round(eager_ms, 4),
