@@ -345,6 +345,54 @@ def layer_parity(layer, world, rank, dev):
                        "rtol 1e-2 / atol 1e-2*RMS"}
 
 
+def paired_layer_parity(layer, world, rank, dev, h_in, res_in, norm_w, slabs0, slabs1, res1, res2, q_cols):
+    """Paired tensor parallelism, layer 0 (a checker only, outside every timed
+    region): every rank checks its own stages against the oracle -- the
+    column-parallel qkv and gate_up slices within 3 bf16 ulp (and rtol 1e-2 /
+    atol 1e-2 * RMS), the new residuals bit for bit, the row-parallel o and
+    down partials within 3 ulp of the oracle of their K slice -- and the slabs
+    every rank received must be identical on every rank."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from oracle import fp8gq_oracle as O
+    f32 = lambda t: t.float().cpu().numpy()  # noqa: E731
+    u8 = lambda t: t.view(torch.uint8).cpu().numpy()  # noqa: E731
+    (_, _, _, wqkv, sqkv, _, _, qkv_o), (_, _, _, wo, so, _, _, _), \
+        (_, _, _, wgu, sgu, _, _, gu_o), (_, _, _, wd, sd, _, _, _) = layer
+    worst, ok, exact_res = 0.0, True, True
+
+    def within(got, exact):
+        nonlocal worst, ok
+        g = f32(got).astype(np.float64)
+        worst = max(worst, float(np.abs(g - exact).max() / O.bf16_ulp_at(float(np.abs(exact).max()))))
+        ok = ok and bool(O.rms_tolerance_ok(g, exact)) and bool(np.all(np.abs(g - exact) <= O.ref_atol(exact, 3.0)))
+
+    _, ex, _, _, r = O.fused_add_rmsnorm_gemv_quant(f32(h_in), f32(res_in), f32(norm_w), u8(wqkv), f32(sqkv))
+    within(qkv_o, ex)
+    exact_res = exact_res and bool(np.array_equal(f32(res1), r))
+    within(slabs0[rank], O.fused_gemv_quant(f32(qkv_o[:, :q_cols]), u8(wo), f32(so))[1])
+    _, ex, _, _, r = O.fused_reduce_add_rmsnorm_gemv_quant([f32(slabs0[q]) for q in range(world)], f32(res1),
+                                                           f32(norm_w), u8(wgu), f32(sgu))
+    within(gu_o, ex)
+    exact_res = exact_res and bool(np.array_equal(f32(res2), r))
+    within(slabs1[rank], O.fused_swiglu_q_gemm(f32(gu_o), u8(wd), f32(sd))[1])
+    same = True
+    for t in (slabs0, slabs1, res1, res2):
+        ref = t.clone()
+        dist.broadcast(ref, src=0)
+        same = same and torch.equal(ref, t)
+    flags = torch.tensor([1.0 if ok else 0.0, 1.0 if exact_res else 0.0, 1.0 if same else 0.0, -worst], device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+    return {"linears": 4, "ok": bool(flags[0].item() == 1.0 and flags[1].item() == 1.0 and flags[2].item() == 1.0),
+            "within_tolerance": bool(flags[0].item() == 1.0), "residuals_exact": bool(flags[1].item() == 1.0),
+            "ranks_identical": bool(flags[2].item() == 1.0), "max_err_ulp": round(-float(flags[3].item()), 3),
+            "ranks_checked": world,
+            "against": "oracle per rank: column-parallel slices (add + RMSNorm prologue over the rank-ordered sum "
+                       "of the slabs) and row-parallel partials of the K slice, layer 0, 3 bf16 ulp + rtol 1e-2 / "
+                       "atol 1e-2*RMS; residuals bit-exact; slabs identical on every rank"}
+
+
 def stack_runner_line(layers, dev, graph_us):
     """The decode chain as one persistent launch (fp8gq.StackRunner) against
     the same chain as 144 routed per-linear launches (CUDA graph of each)."""
@@ -401,8 +449,11 @@ def run_ours(args):
     layers = []
     xs_len = sum(K for _, K, _ in SHAPES)
     out_len = sum(N for _, _, N in SHAPES)
-    x_all = torch.empty(LAYERS, xs_len, dtype=torch.bfloat16, device=dev)
-    out_all = torch.empty(LAYERS, out_len, dtype=torch.bfloat16, device=dev)
+    # two copies of the step's inputs and outputs: copy 0 is the one the timed
+    # CUDA graph uses; the end-to-end loop alternates between them (see e2e)
+    x_all2 = torch.empty(2, LAYERS, xs_len, dtype=torch.bfloat16, device=dev)
+    out_all2 = torch.empty(2, LAYERS, out_len, dtype=torch.bfloat16, device=dev)
+    x_all, out_all = x_all2[0], out_all2[0]
     shard_all = torch.empty(LAYERS, out_len // world, dtype=torch.bfloat16, device=dev)
     g = torch.Generator(device=dev).manual_seed(7)
     for L in range(LAYERS):
@@ -430,7 +481,7 @@ def run_ours(args):
     pg = None
     if world > 1 and args.tp_mode == "gather":
         from fp8gq.dist import PeerGather
-        pg = PeerGather(out_all.view(-1))
+        pg = PeerGather(out_all2.view(-1))
         # descriptors of every linear's output slice, built once (each call
         # waits for the previous linear's slices, as a decoder's next linear
         # would for its input)
@@ -494,10 +545,16 @@ def run_ours(args):
         if pg is not None:
             pg.wait(layers[-1][-1][6])      # the step ends when the last slices have landed
 
-    def prepared_step_list():
+    def at_parity(t, base2, parity):
+        """The view of base2[parity] at the place t has in base2[0]."""
+        off = (t.data_ptr() - base2[0].data_ptr()) // t.element_size()
+        return base2[parity].view(-1)[off:off + t.numel()].view(t.shape)
+
+    def prepared_step_list(parity=0):
         """The same step as prepared launches (fp8gq.prepared): every call
-        recorded once, the whole step issued by one C call per run.  None for
-        the NCCL mode (its all-gathers are not library launches)."""
+        recorded once, the whole step issued by one C call per run; parity 1
+        runs it on the second copy of the inputs and outputs.  None for the
+        NCCL mode (its all-gathers are not library launches)."""
         plans = []
         if paired:
             for L, lin in enumerate(layers):
@@ -517,12 +574,15 @@ def run_ours(args):
         elif world == 1:
             for lin in layers:
                 for (name, K, N, wq, ws, x, out, shard) in lin:
-                    plans.append(fp8gq.prepare_fused_gemv_quant(x, wq, ws, out=out))
+                    plans.append(fp8gq.prepare_fused_gemv_quant(at_parity(x, x_all2, parity), wq, ws,
+                                                                out=at_parity(out, out_all2, parity)))
         elif pg is not None:
             for li, lin in enumerate(layers):
                 for i, (name, K, N, wq, ws, x, out, shard) in enumerate(lin):
-                    plans.append(pg.prepare_linear(x, wq, ws, out, desc=descs[li][i]))
-            plans.append(pg.prepare_wait(layers[-1][-1][6]))
+                    o = at_parity(out, out_all2, parity)
+                    d = descs[li][i] if parity == 0 else pg.descriptor(o, rank * (N // world), True)
+                    plans.append(pg.prepare_linear(at_parity(x, x_all2, parity), wq, ws, o, desc=d))
+            plans.append(pg.prepare_wait(at_parity(layers[-1][-1][6], out_all2, parity)))
         else:
             return None
         return fp8gq.LaunchList(plans)
@@ -545,7 +605,11 @@ def run_ours(args):
             dist.all_reduce(f, op=dist.ReduceOp.MIN)
             prepared_same = bool(f.item() == 1.0)
     # the outputs of the warm-up steps, checked before anything is timed
-    parity = None if paired else layer_parity(layers[0], world, rank, dev)
+    if paired:
+        parity = paired_layer_parity(layers[0], world, rank, dev, h_in, res_buf[0, 1], norm_w, slabs[0, 0],
+                                     slabs[0, 1], res_buf[1, 0], res_buf[1, 1], q_cols)
+    else:
+        parity = layer_parity(layers[0], world, rank, dev)
     barrier()
 
     graph = torch.cuda.CUDAGraph()
@@ -774,77 +838,63 @@ def run_ours(args):
         return ms_
 
     def e2e_pipelined_ms():
-        """The prepared step with each layer's input copied in on one copy
-        stream and its outputs copied out on another, ordered by events, so
-        the copies of one layer overlap the linears of the others (the same
-        bytes as the serial loop; every copy inside the timed region).  A
-        layer's gathered outputs are complete once the next layer's first
-        linear has waited for them (the last layer's: after the step's final
-        wait), so that is where its copy out starts."""
+        """The prepared step with the copies overlapped, through two copies of
+        the step's buffers: step k runs on copy k % 2, its inputs are copied in
+        (one stream) while step k - 1 runs, and its outputs copied out (another
+        stream) while step k + 1 runs.  The compute stream waits twice per step
+        -- for its inputs before the first layer, and before the last layer for
+        the copy out of step k - 1 (same copy as step k + 1), which is also the
+        point after which the other ranks may store step k + 1's slices into
+        it -- so the chain of launches is not broken at every layer.  Every
+        step's copies, in and out, are inside the timed region."""
         if paired or prepared is None:
             return None
         npl = len(SHAPES)
-        per_layer = [fp8gq.LaunchList(prepared.plans[npl * L:npl * (L + 1)]) for L in range(LAYERS)]
-        tail = fp8gq.LaunchList(prepared.plans[npl * LAYERS:]) if len(prepared.plans) > npl * LAYERS else None
+        lists = []
+        for parity in (0, 1):
+            full = prepared if parity == 0 else prepared_step_list(1)
+            lists.append((fp8gq.LaunchList(full.plans[:npl * (LAYERS - 1)]),
+                          fp8gq.LaunchList(full.plans[npl * (LAYERS - 1):])))
         comp = torch.cuda.current_stream(dev)
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        ev = lambda: torch.cuda.Event()  # noqa: E731
-        in_ready, in_free = [ev() for _ in range(LAYERS)], [ev() for _ in range(LAYERS)]
-        out_ready, out_free = [ev() for _ in range(LAYERS)], [ev() for _ in range(LAYERS)]
+        in_ready = [torch.cuda.Event(), torch.cuda.Event()]
+        step_done = [torch.cuda.Event(), torch.cuda.Event()]
+        out_free = [torch.cuda.Event(), torch.cuda.Event()]
         h_in, h_out = hosts_in[0], hosts_out[0]
-        done = ev()
+        start_gate = torch.cuda.Event()
 
-        def copy_out(L):
+        def enqueue(k, gate=None):
+            q = k % 2
+            with torch.cuda.stream(s_in):
+                if gate is not None:
+                    s_in.wait_event(gate)
+                if k >= 2:
+                    s_in.wait_event(step_done[q])        # step k - 2 is done with copy q's inputs
+                x_all2[q].copy_(h_in, non_blocking=True)
+                in_ready[q].record(s_in)
+            comp.wait_event(in_ready[q])
+            head, tail = lists[q]
+            head.run()
+            if k >= 1:
+                comp.wait_event(out_free[(k - 1) % 2])   # step k - 1's outputs are copied out
+            tail.run()
+            step_done[q].record(comp)
             with torch.cuda.stream(s_out):
-                s_out.wait_event(out_ready[L])
-                h_out[L].copy_(out_all[L], non_blocking=True)
-                out_free[L].record(s_out)
+                s_out.wait_event(step_done[q])
+                h_out.copy_(out_all2[q], non_blocking=True)
+                out_free[q].record(s_out)
 
-        def one_step(first):
-            for L in range(LAYERS):
-                with torch.cuda.stream(s_in):
-                    if not first:
-                        s_in.wait_event(in_free[L])          # the last step's linears of layer L have read it
-                    x_all[L].copy_(h_in[L], non_blocking=True)
-                    in_ready[L].record(s_in)
-            for L in range(LAYERS):
-                comp.wait_event(in_ready[L])
-                # out_all[L] is read by the last step's copy out: this rank
-                # rewrites its slice in layer L, and with peer stores the
-                # other ranks rewrite theirs once this rank has finished its
-                # call before layer L (its layer L - 1; for layer 0 the step's
-                # last layer) -- so those layers wait for that copy out too
-                if not first:
-                    comp.wait_event(out_free[L])
-                if world > 1 and L + 1 < LAYERS and not first:
-                    comp.wait_event(out_free[L + 1])
-                if world > 1 and L == LAYERS - 1:
-                    comp.wait_event(out_free[0])             # recorded earlier in this step
-                per_layer[L].run()
-                in_free[L].record(comp)
-                if world == 1:
-                    out_ready[L].record(comp)
-                    copy_out(L)
-                elif L > 0:
-                    out_ready[L - 1].record(comp)            # layer L waited for every slice of layer L - 1
-                    copy_out(L - 1)
-            if tail is not None:
-                tail.run()
-            if world > 1:
-                out_ready[LAYERS - 1].record(comp)
-                copy_out(LAYERS - 1)
-            done.record(s_out)
-
+        for k in range(2):                               # fill the pipeline
+            enqueue(k)
+        comp.wait_event(out_free[1])
+        torch.cuda.synchronize()
+        barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        one_step(True)
-        for it in range(2 + args.e2e_steps):
-            if it == 2:
-                comp.wait_event(done)
-                torch.cuda.synchronize()
-                barrier()
-                e0.record(comp)
-            one_step(False)
-        comp.wait_event(done)
+        e0.record(comp)
+        start_gate.record(comp)
+        for k in range(2, 2 + args.e2e_steps):
+            enqueue(k, gate=start_gate if k == 2 else None)
+        comp.wait_event(out_free[(1 + args.e2e_steps) % 2])
         e1.record(comp)
         torch.cuda.synchronize()
         ms_ = e0.elapsed_time(e1) / args.e2e_steps
@@ -869,8 +919,9 @@ def run_ours(args):
            "path": (("fp8gq.LaunchList of prepared " + ("PeerGather paired linears" if paired else
                                                           "PeerGather.prepare_linear calls" if pg is not None else
                                                           "fp8gq.prepare_fused_gemv_quant calls") +
-                     (", one LaunchList run per layer, each layer's copies in and out on two copy streams "
-                      "overlapping the other layers' linears (eager, no graph)" if piped_ms is not None else
+                     (", two copies of the step's buffers: each step's inputs copied in while the step before "
+                      "runs and its outputs copied out while the step after runs, on two copy streams (eager, "
+                      "no graph)" if piped_ms is not None else
                       ", one run per step, copies before and after it (eager, no graph)"))
                     if prepared is not None else "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
            "serial_copies": {"ms_per_step": round(serial_ms, 4),

@@ -156,6 +156,10 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   if (K > kRowMaxK) return FP8GQ_ERR_UNSUPPORTED;
   const int n_chunks = K / 16;
   const int c_need = (n_chunks + 383) / 384;
+  // rows per ring stage: the most (4, 2 or 1) whose stage is at most 16 KB
+  // (fewer rows per stage cost more per byte than their better balance over
+  // the CTAs saves: measured on B200, o_proj 4096 x 4096 takes 6.8 us with
+  // 4-row stages and 7.5 us with 2-row stages)
   int ri = 2;
   while (ri > 0 && kRowRs[ri] * K > 16384) --ri;
   const int R = kRowRs[ri];
