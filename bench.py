@@ -95,13 +95,16 @@ def parse():
                     help="1 (default): declare the weights static (fp8gq.set_static_weights) -- no work "
                          "queued before a linear writes its weights, as in any decode step -- letting each "
                          "kernel fetch its first weight tiles before the previous one finishes; 0: do not")
-    ap.add_argument("--tp-mode", choices=["paired", "gather", "nccl"], default="gather",
+    ap.add_argument("--tp-mode", choices=["paired", "gather", "tagged", "nccl"], default="gather",
                     help="N > 1: paired -- qkv and gate_up column-parallel, o and down "
                          "row-parallel; each row-parallel kernel stores its partial into every rank's "
                          "slab over NVLink and the next column-parallel kernel adds the slabs in its "
                          "add + RMSNorm prologue (two exchanges per layer); gather (default) -- every "
-                         "linear N-sharded, the kernels store their output slices into every rank's buffer; "
-                         "nccl -- every linear N-sharded, an NCCL all-gather after each")
+                         "linear N-sharded, the kernels store their output slices into every rank's buffer "
+                         "and raise a flag; tagged -- the same stores as tagged words, each linear reading "
+                         "the previous one's output (qkv -> o -> gate_up -> down -> next qkv) and polling "
+                         "the words it reads, no flags; nccl -- every linear N-sharded, an NCCL all-gather "
+                         "after each")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
@@ -443,6 +446,7 @@ def run_ours(args):
             dist.barrier()
 
     paired = world > 1 and args.tp_mode == "paired"
+    tagged = world > 1 and args.tp_mode == "tagged"
     # ---- operands: each rank owns rows [r*N/world, (r+1)*N/world) of every
     # linear (gather / nccl modes), or, paired, rows of qkv and gate_up and
     # columns [r*K/world, (r+1)*K/world) of o and down
@@ -487,6 +491,42 @@ def run_ours(args):
         # would for its input)
         descs = [[pg.descriptor(lin[i][6], rank * (lin[i][2] // world), True) for i in range(len(SHAPES))]
                  for lin in layers]
+    def at_parity(t, base2, parity):
+        """The view of base2[parity] at the place t has in base2[0]."""
+        off = (t.data_ptr() - base2[0].data_ptr()) // t.element_size()
+        return base2[parity].view(-1)[off:off + t.numel()].view(t.shape)
+
+    if tagged:
+        # Tagged words: the step is a chain -- layer L's qkv reads layer L-1's
+        # down output (layer 0: the step input, bf16), o the first 4096
+        # columns of qkv's output (the attention stand-in), gate_up o's
+        # output, down the first 12288 columns of gate_up's output -- every
+        # input a tagged output of the linear before it, polled word by word
+        # by the kernel that reads it.  A decode kernel turns the last
+        # output into the step's bf16 result.  Two copies of the words for the
+        # pipelined end-to-end loop.
+        from fp8gq.dist import PeerGather
+        words2 = torch.zeros(2, LAYERS, out_len // 2, dtype=torch.int64, device=dev)
+        pg = PeerGather(words2.view(-1), tagged=True)
+        dec2 = torch.empty(2, 1, SHAPES[-1][2], dtype=torch.bfloat16, device=dev)
+
+        def chain_io(q):
+            """[(input, output words, waits for its input)] per linear, copy q."""
+            io, prev = [], None
+            for L, lin in enumerate(layers):
+                outs, oo = [], 0
+                for name, K, N in SHAPES:
+                    outs.append(words2[q, L, oo // 2:(oo + N) // 2].view(1, N // 2))
+                    oo += N
+                ins = [at_parity(lin[0][5], x_all2, q) if prev is None else prev,
+                       outs[0][:, :SHAPES[1][1] // 2], outs[1], outs[2][:, :SHAPES[3][1] // 2]]
+                for i in range(len(SHAPES)):
+                    io.append((ins[i], outs[i], not (L == 0 and i == 0)))
+                prev = outs[3]
+            return io
+        tagged_io = [chain_io(0), chain_io(1)]
+        tdescs = [[pg.descriptor(o, rank * (SHAPES[k % len(SHAPES)][2] // world), w)
+                   for k, (_, o, w) in enumerate(io)] for io in tagged_io]
     if paired:
         # Paired tensor parallelism, layer by layer:
         #   qkv      column-parallel, add + RMSNorm prologue over the sum of the
@@ -533,6 +573,13 @@ def run_ours(args):
         if paired:
             paired_step()
             return
+        if tagged:
+            io = tagged_io[0]
+            for k, (x, o, w) in enumerate(io):
+                lin = layers[k // len(SHAPES)][k % len(SHAPES)]
+                pg.linear(x, lin[3], lin[4], o, desc=tdescs[0][k])
+            pg.decode(io[-1][1], dec2[0])       # the step ends when the last slices have landed
+            return
         for li, lin in enumerate(layers):
             for i, (name, K, N, wq, ws, x, out, shard) in enumerate(lin):
                 if world == 1:
@@ -545,18 +592,19 @@ def run_ours(args):
         if pg is not None:
             pg.wait(layers[-1][-1][6])      # the step ends when the last slices have landed
 
-    def at_parity(t, base2, parity):
-        """The view of base2[parity] at the place t has in base2[0]."""
-        off = (t.data_ptr() - base2[0].data_ptr()) // t.element_size()
-        return base2[parity].view(-1)[off:off + t.numel()].view(t.shape)
-
     def prepared_step_list(parity=0):
         """The same step as prepared launches (fp8gq.prepared): every call
         recorded once, the whole step issued by one C call per run; parity 1
         runs it on the second copy of the inputs and outputs.  None for the
         NCCL mode (its all-gathers are not library launches)."""
         plans = []
-        if paired:
+        if tagged:
+            io = tagged_io[parity]
+            for k, (x, o, w) in enumerate(io):
+                lin = layers[k // len(SHAPES)][k % len(SHAPES)]
+                plans.append(pg.prepare_linear(x, lin[3], lin[4], o, desc=tdescs[parity][k]))
+            plans.append(pg.prepare_decode(io[-1][1], dec2[parity]))
+        elif paired:
             for L, lin in enumerate(layers):
                 (_, _, _, wqkv, sqkv, _, _, qkv_o), (_, _, _, wo, so, _, _, _), \
                     (_, _, _, wgu, sgu, _, _, gu_o), (_, _, _, wd, sd, _, _, _) = lin
@@ -594,12 +642,22 @@ def run_ours(args):
     # the prepared form of the step must leave the same outputs as the calls
     prepared = prepared_step_list()
     prepared_same = None
+
+    def step_outputs():
+        """What a step leaves (tagged: the words' values, whose tags advance
+        with every call, and the decoded result)."""
+        if paired:
+            return [res_buf.clone(), slab_buf.clone()]
+        if tagged:
+            from fp8gq.dist import untag
+            return [untag(words2[0]), dec2[0].clone()]
+        return [out_all.clone()]
     if prepared is not None:
-        final = [t.clone() for t in ([res_buf, slab_buf] if paired else [out_all])]
+        final = step_outputs()
         prepared.run()
         torch.cuda.synchronize()
         barrier()
-        prepared_same = all(torch.equal(a, b) for a, b in zip(final, [res_buf, slab_buf] if paired else [out_all]))
+        prepared_same = all(torch.equal(a, b) for a, b in zip(final, step_outputs()))
         if world > 1:
             f = torch.tensor([1.0 if prepared_same else 0.0], device=dev)
             dist.all_reduce(f, op=dist.ReduceOp.MIN)
@@ -608,6 +666,30 @@ def run_ours(args):
     if paired:
         parity = paired_layer_parity(layers[0], world, rank, dev, h_in, res_buf[0, 1], norm_w, slabs[0, 0],
                                      slabs[0, 1], res_buf[1, 0], res_buf[1, 1], q_cols)
+    elif tagged:
+        # layer 0 as bf16 (inputs and outputs decoded from their words), and
+        # the words' sequence numbers: one per output, consecutive along the
+        # chain, the same on every rank
+        from fp8gq.dist import tags, untag
+        io = tagged_io[0]
+        dec_layer, seqs = [], []
+        for i, (name, K, N, wq, ws, x, out, shard) in enumerate(layers[0]):
+            xin, o, _ = io[i]
+            xb = xin if xin.dtype == torch.bfloat16 else untag(xin)
+            dec_layer.append((name, K, N, wq, ws, xb, untag(o), shard))
+            tg = tags(o)
+            seqs.append(int(tg.flatten()[0]) if bool((tg == tg.flatten()[0]).all()) else -1)
+        parity = layer_parity(dec_layer, world, rank, dev)
+        tag_ok = all(t > 0 for t in seqs) and all(seqs[i + 1] == seqs[i] + 1 for i in range(len(seqs) - 1))
+        st = torch.tensor(seqs, dtype=torch.int64, device=dev)
+        st0 = st.clone()
+        dist.broadcast(st0, src=0)
+        f = torch.tensor([1.0 if (tag_ok and torch.equal(st, st0)) else 0.0], device=dev)
+        dist.all_reduce(f, op=dist.ReduceOp.MIN)
+        parity["tags_consistent"] = bool(f.item() == 1.0)
+        parity["ok"] = parity["ok"] and parity["tags_consistent"]
+        parity["against"] += ("; tagged words decoded, every word of an output carrying one sequence number, "
+                              "consecutive along the chain and equal on every rank")
     else:
         parity = layer_parity(layers[0], world, rank, dev)
     barrier()
@@ -807,8 +889,13 @@ def run_ours(args):
     # (paired: the step's input hidden state and residual in, the last
     # layer's down partials and residual out; otherwise every linear's input
     # in and every output out)
-    e2e_in = [h_in, res_buf[0, 1]] if paired else [x_all]
-    e2e_out = [slabs[LAYERS - 1, 1], res_buf[LAYERS, 1]] if paired else [out_all]
+    # (tagged: the step's input in, its decoded result out -- the chain
+    # carries everything else)
+    if tagged:
+        e2e_in, e2e_out = [layers[0][0][5]], [dec2[0]]
+    else:
+        e2e_in = [h_in, res_buf[0, 1]] if paired else [x_all]
+        e2e_out = [slabs[LAYERS - 1, 1], res_buf[LAYERS, 1]] if paired else [out_all]
     hosts_in = [torch.empty_like(t, device="cpu").pin_memory() for t in e2e_in]
     for t, h in zip(e2e_in, hosts_in):
         h.copy_(t.cpu())
@@ -870,7 +957,7 @@ def run_ours(args):
                     s_in.wait_event(gate)
                 if k >= 2:
                     s_in.wait_event(step_done[q])        # step k - 2 is done with copy q's inputs
-                x_all2[q].copy_(h_in, non_blocking=True)
+                (at_parity(layers[0][0][5], x_all2, q) if tagged else x_all2[q]).copy_(h_in, non_blocking=True)
                 in_ready[q].record(s_in)
             comp.wait_event(in_ready[q])
             head, tail = lists[q]
@@ -881,7 +968,7 @@ def run_ours(args):
             step_done[q].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(step_done[q])
-                h_out.copy_(out_all2[q], non_blocking=True)
+                h_out.copy_(dec2[q] if tagged else out_all2[q], non_blocking=True)
                 out_free[q].record(s_out)
 
         for k in range(2):                               # fill the pipeline
@@ -917,6 +1004,8 @@ def run_ours(args):
            "d2h_bytes_per_step": sum(t.numel() * t.element_size() for t in e2e_out),
            "ms_per_step": round(e2e_ms, 4),
            "path": (("fp8gq.LaunchList of prepared " + ("PeerGather paired linears" if paired else
+                                                          "PeerGather.prepare_linear calls on tagged words "
+                                                          "(the step input in, the decoded result out)" if tagged else
                                                           "PeerGather.prepare_linear calls" if pg is not None else
                                                           "fp8gq.prepare_fused_gemv_quant calls") +
                      (", two copies of the step's buffers: each step's inputs copied in while the step before "
@@ -958,6 +1047,10 @@ def run_ours(args):
                                             "o, down row-parallel; partials stored into every rank's slab by "
                                             "the kernels over NVLink and summed in the next linear's add + "
                                             "RMSNorm prologue") if paired else
+                                           (f"N-sharded x{world}, output slices stored into every rank by the "
+                                            "kernels over NVLink as tagged words (each linear reading the "
+                                            "previous one's output: qkv -> o -> gate_up -> down -> next qkv), "
+                                            "no flags") if tagged else
                                            (f"N-sharded x{world}, output slices stored into every rank by the "
                                             "kernels over NVLink") if pg is not None else
                                            f"N-sharded x{world} + NCCL all-gather per linear") if world > 1

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define FP8GQ_VERSION 1
+#define FP8GQ_VERSION 2
 
 enum fp8gq_status {
     FP8GQ_OK = 0,
@@ -152,7 +152,25 @@ typedef struct fp8gq_gather {
     int wait_input;
     int local_out;                           /* 1: only wait; the output stays local
                                                 (set by the reduce entry point below) */
+    int tagged;                              /* 1: tagged words, see below */
 } fp8gq_gather;
+
+/* Tagged words (tagged = 1), the low-latency form of the same gather.  The
+ * flags above cost the publishing kernel a system-scope fence -- a wait for
+ * every one of its NVLink stores to be acknowledged -- and a second round of
+ * peer stores.  With tagged = 1 every stored word carries its own proof of
+ * arrival instead: a 64-bit word holds columns 2i and 2i + 1 of a row (bf16,
+ * low half first) and, in its high 32 bits, the sequence number of the call
+ * that wrote it.  out[r] then points at rank r's words: M x ldo / 2 uint64
+ * (ldo and col0 in elements, as above; ldo a multiple of 8, out[r] 16-byte
+ * aligned).  A call with wait_input reads its activation as such words (x or
+ * gu points at words, ldx / ldgu in elements) and polls each word it reads,
+ * bounded, until it carries this rank's last sequence number: the input must
+ * be the output of this rank's last publishing call.  A publishing call
+ * without wait_input first waits until every rank has finished this rank's
+ * previous publishing call (each rank's own slot flags[q][q], raised without a
+ * fence).  M <= 16 (one launch per call); no norm prologue; local_out = 0.
+ * fp8gq_gather_decode turns a tagged output into bf16. */
 
 /* fp8gq_fused_gemv_quant with the output gathered as above (routing and
  * workspace as fp8gq_fused_gemv_quant; N is this rank's slice width). */
@@ -165,6 +183,15 @@ int fp8gq_fused_gemv_quant_gather(const void *x, int64_t ldx, const void *w, int
  * this rank's last gathered output has arrived -- e.g. before the full output
  * is read by something that is not a gathered call with wait_input set. */
 int fp8gq_gather_wait(const fp8gq_gather *gather, fp8gq_stream_t stream);
+
+/* Tagged words: waits on `stream` (bounded) until every word of this rank's
+ * full tagged output [M, N] -- gather->out[gather->rank], row stride
+ * gather->ldo elements -- carries this rank's last sequence number, and
+ * writes the values as bf16 [M, N] into out (row stride ldo elements; out
+ * 16-byte aligned, ldo a multiple of 8).  fp8gq_gather_wait is for flags only
+ * (FP8GQ_ERR_UNSUPPORTED with tagged = 1). */
+int fp8gq_gather_decode(const fp8gq_gather *gather, int M, int N, void *out, int64_t ldo,
+                        fp8gq_stream_t stream);
 
 /* Tensor-parallel pairing without a gather in between: a column-parallel
  * (N-sharded) linear keeps its output slice on its rank, where it feeds a
@@ -427,6 +454,8 @@ int fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant(const void *x, int nsrc, i
                                                       float *sx_out, const fp8gq_gather *wait, void *workspace,
                                                       size_t workspace_bytes, fp8gq_launch_plan *plan);
 int fp8gq_prepare_gather_wait(const fp8gq_gather *gather, fp8gq_launch_plan *plan);
+int fp8gq_prepare_gather_decode(const fp8gq_gather *gather, int M, int N, void *out, int64_t ldo,
+                                fp8gq_launch_plan *plan);
 int fp8gq_launch_plans(const fp8gq_launch_plan *plans, int n, fp8gq_stream_t stream);
 
 /* fp8gq_gemv_quant_tm without a workspace argument.  No counterpart in the

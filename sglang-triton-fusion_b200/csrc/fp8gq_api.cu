@@ -215,7 +215,9 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
   p.early_weights = g_static_weights.load(std::memory_order_relaxed);
   // at most two CTAs per SM, and never more than are resident at once
   int grid = (per_sm < 2 ? per_sm : 2) * di.sm_count;
-  if (grid > p.n_groups) grid = p.n_groups;
+  // tagged words with one row per group: the CTAs take rows in pairs
+  const int units = (R == 1 && gather && gather->tagged) ? p.n_groups / 2 : p.n_groups;
+  if (grid > units) grid = units;
   if (launch_with_pdl(fn, dim3(grid), dim3(T + 32), smem, stream, p) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
   return launch_status();
 }
@@ -290,7 +292,56 @@ int to_gather_params(const fp8gq_gather* gather, GatherParams* g) {
   g->rank = gather->rank;
   g->wait_input = gather->wait_input ? 1 : 0;
   g->local_out = gather->local_out ? 1 : 0;
+  g->tagged = gather->tagged ? 1 : 0;
+  if (g->tagged) {
+    // words of two columns: even col0 and ldo (16-byte rows), aligned buffers
+    if (g->local_out) return FP8GQ_ERR_UNSUPPORTED;
+    if ((gather->ldo % 8) || (gather->col0 % 2)) return FP8GQ_ERR_ALIGNMENT;
+    for (int r = 0; r < gather->world; ++r)
+      if (reinterpret_cast<uintptr_t>(gather->out[r]) & 15u) return FP8GQ_ERR_ALIGNMENT;
+  }
   return FP8GQ_OK;
+}
+
+// This rank's own output slice (for the shape checks and the plain-output
+// argument): element col0 of its full output, or its word for tagged words.
+void* own_slice(const fp8gq_gather* gather) {
+  if (gather->tagged) return static_cast<uint64_t*>(gather->out[gather->rank]) + gather->col0 / 2;
+  return static_cast<__nv_bfloat16*>(gather->out[gather->rank]) + gather->col0;
+}
+
+// A tagged call: one launch (M <= 16); a waited-for input is read as words
+// (16-byte aligned rows of ld / 2 words).
+int check_tagged(const fp8gq_gather* gather, const void* x, int64_t ldx, int M) {
+  if (!gather->tagged) return FP8GQ_OK;
+  if (M > 16) return FP8GQ_ERR_UNSUPPORTED;
+  if (gather->wait_input && ((reinterpret_cast<uintptr_t>(x) & 15u) || (ldx % 8))) return FP8GQ_ERR_ALIGNMENT;
+  return FP8GQ_OK;
+}
+
+// Tagged words -> bf16: each thread polls 8 words (16 columns of a row) of
+// this rank's full output until they carry its last sequence number.
+__global__ void gather_decode_kernel(const GatherParams g, __nv_bfloat16* out, int64_t ldo, int M, int N) {
+  grid_dependency_wait();
+  const unsigned int tag = gather_seq_now(g);
+  const uint64_t* words = reinterpret_cast<const uint64_t*>(g.out[g.rank]);
+  const int per_row = N / 16;
+  const int64_t total = static_cast<int64_t>(M) * per_row;
+  bool live = true;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = i / per_row;
+    const int64_t c = i - m * per_row;
+    const uint64_t* w = words + ((m * g.ldo) >> 1) + 8 * c;
+    uint64_t v[8];
+    uint32_t xw[8];
+    tagged_issue8(w, v);
+    tagged_finish8(w, tag, v, xw, live);
+    uint4* o = reinterpret_cast<uint4*>(out + m * ldo + 16 * c);
+    o[0] = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+    o[1] = make_uint4(xw[4], xw[5], xw[6], xw[7]);
+  }
+  grid_launch_dependents();
 }
 
 using AddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
@@ -480,6 +531,7 @@ int fp8gq_fused_reduce_add_rmsnorm_gemv_quant(const void* x, int nsrc, int64_t s
   GatherParams g{};
   if (wait) {
     // only the input wait: flags, seq, world and rank of the descriptor
+    if (wait->tagged) return FP8GQ_ERR_UNSUPPORTED;   // the norm prologue reads bf16 sources
     if (!wait->seq) return FP8GQ_ERR_NULL_POINTER;
     if (wait->world < 2 || wait->world > FP8GQ_MAX_GATHER_RANKS || wait->rank < 0 || wait->rank >= wait->world)
       return FP8GQ_ERR_SHAPE;
@@ -533,8 +585,10 @@ int fp8gq_fused_gemv_quant_gather(const void* x, int64_t ldx, const void* w, int
   if (st != FP8GQ_OK) return st;
   if (gather->ldo < static_cast<int64_t>(gather->col0) + N) return FP8GQ_ERR_STRIDE;
   // the rank's own output slice stands in for `out` in the shape checks
-  void* own = static_cast<__nv_bfloat16*>(gather->out[gather->rank]) + gather->col0;
+  void* own = own_slice(gather);
   st = check_common(x, w, ws, own, M, N, K, ldw, ldws, gather->ldo);
+  if (st != FP8GQ_OK) return st;
+  st = check_tagged(gather, x, ldx, M);
   if (st != FP8GQ_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (M == 1 && m1_uses_row(N, K)) return launch_row(false, x, w, ldw, ws, ldws, own, N, K, nullptr, nullptr, s, &g);
@@ -554,8 +608,10 @@ int fp8gq_fused_swiglu_q_gemm_gather(const void* gu, int64_t ldgu, const void* w
   int st = to_gather_params(gather, &g);
   if (st != FP8GQ_OK) return st;
   if (gather->ldo < static_cast<int64_t>(gather->col0) + N) return FP8GQ_ERR_STRIDE;
-  void* own = static_cast<__nv_bfloat16*>(gather->out[gather->rank]) + gather->col0;
+  void* own = own_slice(gather);
   st = check_common(gu, w, ws, own, M, N, I, ldw, ldws, gather->ldo);
+  if (st != FP8GQ_OK) return st;
+  st = check_tagged(gather, gu, ldgu, M);
   if (st != FP8GQ_OK) return st;
   if (ldgu < 2 * static_cast<int64_t>(I)) return FP8GQ_ERR_STRIDE;
   if (ldgu % 8) return FP8GQ_ERR_ALIGNMENT;
@@ -573,7 +629,29 @@ int fp8gq_gather_wait(const fp8gq_gather* gather, fp8gq_stream_t stream) {
   GatherParams g;
   int st = to_gather_params(gather, &g);
   if (st != FP8GQ_OK) return st;
+  if (g.tagged) return FP8GQ_ERR_UNSUPPORTED;   // tagged words: fp8gq_gather_decode
   if (launch_with_pdl(gather_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), g) != cudaSuccess)
+    return FP8GQ_ERR_LAUNCH;
+  return launch_status();
+}
+
+int fp8gq_gather_decode(const fp8gq_gather* gather, int M, int N, void* out, int64_t ldo, fp8gq_stream_t stream) {
+  GatherParams g;
+  int st = to_gather_params(gather, &g);
+  if (st != FP8GQ_OK) return st;
+  if (!g.tagged) return FP8GQ_ERR_UNSUPPORTED;   // flags: fp8gq_gather_wait
+  if (!out) return FP8GQ_ERR_NULL_POINTER;
+  if (M < 1 || N <= 0 || N % kGroup) return FP8GQ_ERR_SHAPE;
+  if (ldo < N || gather->ldo < N) return FP8GQ_ERR_STRIDE;
+  if (!aligned16(out) || (ldo % 8)) return FP8GQ_ERR_ALIGNMENT;
+  DeviceInfo di;
+  st = device_info(&di, nullptr);
+  if (st != FP8GQ_OK) return st;
+  const int64_t chunks = static_cast<int64_t>(M) * (N / 16);
+  int64_t blocks = (chunks + 255) / 256;
+  if (blocks > di.sm_count) blocks = di.sm_count;
+  if (launch_with_pdl(gather_decode_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), g, static_cast<__nv_bfloat16*>(out), ldo, M, N) != cudaSuccess)
     return FP8GQ_ERR_LAUNCH;
   return launch_status();
 }
@@ -1016,6 +1094,11 @@ int fp8gq_prepare_fused_reduce_add_rmsnorm_gemv_quant(
 
 int fp8gq_prepare_gather_wait(const fp8gq_gather* gather, fp8gq_launch_plan* plan) {
   return prepare_into(plan, [&] { return fp8gq_gather_wait(gather, nullptr); });
+}
+
+int fp8gq_prepare_gather_decode(const fp8gq_gather* gather, int M, int N, void* out, int64_t ldo,
+                                fp8gq_launch_plan* plan) {
+  return prepare_into(plan, [&] { return fp8gq_gather_decode(gather, M, N, out, ldo, nullptr); });
 }
 
 int fp8gq_launch_plans(const fp8gq_launch_plan* plans, int n, fp8gq_stream_t stream) {

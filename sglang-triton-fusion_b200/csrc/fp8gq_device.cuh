@@ -380,8 +380,29 @@ constexpr int kMaxGatherRanks = 8;
 // partials, col0 = 0.  A kernel with local_out set only waits (wait_input) and
 // writes its own output locally, publishing nothing: the column-parallel
 // linear that reduces those partials in its prologue.
+//
+// Tagged words (tagged = 1): the flags above cost a system-scope fence in the
+// last CTA of every publishing kernel (it waits for every NVLink store of the
+// kernel to be acknowledged) and a second round of peer stores after it.
+// With tagged words each store carries its own proof of arrival instead: a
+// 64-bit word holds two bf16 outputs (columns 2i, 2i + 1 of a row; low half
+// first) and, in its high 32 bits, the sequence number of the kernel that
+// wrote it, stored with one single-copy-atomic 64-bit store.  The buffers
+// hold M x ldo / 2 words.  A kernel whose input is a tagged output
+// (wait_input) polls the very words it reads until each carries the
+// sequence number of this rank's last publishing kernel; no fence and no flag
+// sits between a producer's stores and its consumer.  Write-after-read needs
+// no wait either when the input is the last gathered output: every output
+// word of the consumer depends on every input word, and each input word from
+// rank q was written after q's kernel had read its own input -- the buffer
+// the consumer is about to overwrite (with two buffers in turn).  A
+// publishing kernel without wait_input instead waits, before its first
+// store, until every rank's own flag slot flags[q][q] -- raised with a local
+// store by q's last CTA, no fence -- shows that q has finished its previous
+// publishing kernel.  Tagged kernels are single launches (M <= 16) whose
+// input, when waited for, is the output of the last publishing kernel.
 struct GatherParams {
-  __nv_bfloat16* out[kMaxGatherRanks];   // rank r's full output [M, ldo], as mapped here
+  __nv_bfloat16* out[kMaxGatherRanks];   // rank r's full output [M, ldo], as mapped here (tagged: words)
   unsigned int* flags[kMaxGatherRanks];  // rank r's flags[world], as mapped here
   unsigned int* counter;                 // this rank: CTAs of the running kernel that are done
   unsigned int* seq;                     // this rank: sequence number of its last gathered kernel
@@ -391,6 +412,7 @@ struct GatherParams {
   int rank;
   int wait_input;
   int local_out;                         // 1: output to the local `out` only, no flags raised
+  int tagged;                            // 1: tagged words, see above
 };
 
 // Whether a kernel's output goes to every rank (and raises the flags).
@@ -409,6 +431,83 @@ __device__ __forceinline__ void gather_store(const GatherParams& g, int64_t m, i
   for (int r = 0; r < g.world; ++r) g.out[r][off] = v;
 }
 
+// ---- tagged words ----------------------------------------------------------
+
+// The sequence number after s (0 is skipped: a zero-filled buffer never
+// carries a valid tag).
+__device__ __forceinline__ unsigned int tag_after(unsigned int s) {
+  const unsigned int t = s + 1u;
+  return t ? t : 1u;
+}
+
+// This rank's last publishing sequence number; read after the grid-dependency
+// wait (the previous publishing kernel's last CTA wrote it).  A publishing
+// kernel tags its words with tag_after() of it; a waiting kernel expects it.
+__device__ __forceinline__ unsigned int gather_seq_now(const GatherParams& g) {
+  return *reinterpret_cast<volatile unsigned int*>(g.seq);
+}
+
+// Output columns n, n + 1 (n even) of token m of this rank's slice as one
+// tagged word, to every rank.
+__device__ __forceinline__ void gather_store_pair(const GatherParams& g, int64_t m, int64_t n, uint32_t pair,
+                                                  unsigned int tag) {
+  const int64_t w = (m * g.ldo + g.col0 + n) >> 1;
+  const uint64_t word = static_cast<uint64_t>(pair) | (static_cast<uint64_t>(tag) << 32);
+#pragma unroll 1
+  for (int r = 0; r < g.world; ++r)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(reinterpret_cast<uint64_t*>(g.out[r]) + w), "l"(word)
+                 : "memory");
+}
+
+// Tagged output element (m, n) held by this lane, with column n + 1 held by
+// the next lane: the even lane stores the pair.  All 32 lanes call it
+// together (the shuffle), with consecutive columns on consecutive lanes.
+__device__ __forceinline__ void gather_store_tagged(const GatherParams& g, int64_t m, int64_t n, __nv_bfloat16 v,
+                                                    unsigned int tag) {
+  const uint32_t lo = __bfloat16_as_ushort(v);
+  const uint32_t hi = __shfl_down_sync(0xffffffffu, lo, 1);
+  if (!(n & 1)) gather_store_pair(g, m, n, lo | (hi << 16), tag);
+}
+
+// Eight tagged words (16 bf16 elements) at w, 16-byte aligned: issue the
+// loads (relaxed, system scope: the words are written by other GPUs).
+__device__ __forceinline__ void tagged_issue8(const uint64_t* w, uint64_t v[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                 : "=l"(v[2 * i]), "=l"(v[2 * i + 1])
+                 : "l"(w + 2 * i)
+                 : "memory");
+}
+
+// The issued words v of tagged_issue8(w): reload until each carries `tag`,
+// then their bf16 pairs into xw.  `live` (per thread) turns false, with the
+// error word set, once the peer limit has passed; later calls of a thread
+// that gave up do not wait again, so a lost peer costs a kernel one limit.
+__device__ __forceinline__ void tagged_finish8(const uint64_t* w, unsigned int tag, uint64_t v[8], uint32_t xw[8],
+                                               bool& live) {
+  auto all_tagged = [&]() {
+    bool ok = true;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ok &= static_cast<unsigned int>(v[e] >> 32) == tag;
+    return ok;
+  };
+  if (live && !all_tagged()) {
+    const uint64_t t0 = global_ns();
+    for (;;) {
+      tagged_issue8(w, v);
+      if (all_tagged()) break;
+      if (global_ns() - t0 > peer_wait_limit_ns()) {
+        record_error(kSiteGather);
+        live = false;
+        break;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) xw[e] = static_cast<uint32_t>(v[e]);
+}
+
 // One thread per CTA, after a barrier that follows every gather_store of the
 // CTA: count the CTA (acq_rel at GPU scope: the barrier puts the CTA's stores
 // before the release); the last one, having acquired every other CTA's count,
@@ -417,7 +516,14 @@ __device__ __forceinline__ void gather_store(const GatherParams& g, int64_t m, i
 __device__ __forceinline__ void gather_cta_done(const GatherParams& g, unsigned int ncta) {
   unsigned int old;
   asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], 1;" : "=r"(old) : "l"(g.counter) : "memory");
-  if (old == ncta - 1u) {
+  if (old == ncta - 1u && g.tagged) {
+    // tagged words: the outputs carry their own sequence number; only the
+    // local counters and this rank's own flag slot change (no fence)
+    *g.counter = 0u;
+    const unsigned int s = tag_after(*g.seq);
+    *g.seq = s;
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(g.flags[g.rank] + g.rank), "r"(s) : "memory");
+  } else if (old == ncta - 1u) {
     *g.counter = 0u;                     // ready for the next gathered kernel on this stream
     const unsigned int s = *g.seq + 1u;
     *g.seq = s;
@@ -456,7 +562,29 @@ __device__ __forceinline__ bool gather_wait_input(const GatherParams& g, int lan
 // publishing kernel.  A kernel with wait_input has made that wait already; for
 // any other publishing kernel this is the same bounded wait.
 __device__ __forceinline__ void gather_wait_store(const GatherParams& g, int lane) {
-  if (gather_publishes(g) && !g.wait_input) gather_wait_input(g, lane);
+  if (!gather_publishes(g) || g.wait_input) return;
+  if (!g.tagged) {
+    gather_wait_input(g, lane);
+    return;
+  }
+  // tagged: lane q watches rank q's own flag slot over NVLink until rank q
+  // has finished this rank's previous publishing kernel
+  const unsigned int s = gather_seq_now(g);
+  bool ok = true;
+  if (lane < g.world) {
+    const unsigned int* flag = g.flags[lane] + lane;
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 0;; ++it) {
+      if (static_cast<int>(ld_acquire_sys_u32(flag) - s) >= 0) break;
+      if ((it & 255u) == 255u && global_ns() - t0 > peer_wait_limit_ns()) {
+        record_error(kSiteGather);
+        ok = false;
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  (void)ok;
 }
 
 // ---------------------------------------------------------------------------

@@ -439,9 +439,18 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // divisions, done before the grid-dependency wait
   const int nb0 = static_cast<int>(u0 / p.KB);
   const int kb0 = static_cast<int>(u0 - static_cast<int64_t>(nb0) * p.KB);
-  // output element (token m, column n of this launch): local, or to every rank
+  // tagged words: the input carries this rank's last sequence number, the
+  // output the one after it (read after the grid-dependency wait)
+  const bool tagged = p.gather.world > 0 && p.gather.tagged;
+  const bool tagged_in = tagged && p.gather.wait_input;
+  unsigned int tag_in = 0u, tag_out = 0u;
+  // output element (token m, column n of this launch): local, or to every
+  // rank (tagged: all 32 lanes together, consecutive columns on consecutive
+  // lanes -- true of every call below)
   auto store_out = [&](int m, int n, __nv_bfloat16 v) {
-    if (gather_publishes(p.gather))
+    if (tagged)
+      gather_store_tagged(p.gather, m, n, v, tag_out);
+    else if (gather_publishes(p.gather))
       gather_store(p.gather, m, n, v);
     else
       p.out[static_cast<int64_t>(m) * p.ldo + n] = v;
@@ -513,7 +522,11 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   }
   grid_dependency_wait();
-  if (p.gather.wait_input) {
+  if (tagged) {
+    tag_in = gather_seq_now(p.gather);
+    tag_out = tag_after(tag_in);
+  }
+  if (p.gather.wait_input && !tagged) {
     // The activation comes from other ranks: the warps that read it wait for
     // every rank's flag -- warps 2-9, and with the streaming feed the TMA warp
     // too (it loads the activation tiles).  Otherwise warps 0 and 1 start the
@@ -643,6 +656,56 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
           float sx;
           const uint4 packed = quant16_octet(v, live, sx);
           if (live) commit(m, r, kb, packed, sx);
+        }
+      } else if (tagged_in) {
+        // Tagged input words (word i of a row holds elements 2i, 2i + 1):
+        // the loads of kPasses passes are issued first, as below, then each
+        // group's words are polled until they carry this rank's last sequence
+        // number.  A thread that gave up does not wait again.
+        constexpr int kPasses = kSwiglu ? 1 : 2;
+        const uint64_t* xw0 = reinterpret_cast<const uint64_t*>(p.x);
+        bool live_in = true;
+        auto words_of = [&](int m, int kb) {
+          return xw0 + ((static_cast<int64_t>(m) * p.ldx + kb * 128 + chunk * 16) >> 1);
+        };
+        for (int g0 = 0; g0 < ngroups; g0 += 32 * kPasses) {
+          uint64_t wv[kPasses][kSwiglu ? 16 : 8];
+#pragma unroll
+          for (int i = 0; i < kPasses; ++i) {
+            const int g = g0 + 32 * i + oct;
+            if (g < ngroups) {
+              int m, r, kb;
+              group_of(g, m, r, kb);
+              tagged_issue8(words_of(m, kb), wv[i]);
+              if constexpr (kSwiglu) tagged_issue8(words_of(m, kb) + p.K / 2, wv[i] + 8);
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < kPasses; ++i) {
+            if (g0 + 32 * i >= ngroups) break;   // uniform across the warp
+            const int g = g0 + 32 * i + oct;
+            const bool live = g < ngroups;
+            int m = 0, r = 0, kb = 0;
+            if (live) group_of(g, m, r, kb);
+            float v[16];
+            if (live) {
+              uint32_t xw[8], uw[8];
+              tagged_finish8(words_of(m, kb), tag_in, wv[i], xw, live_in);
+              if constexpr (kSwiglu) tagged_finish8(words_of(m, kb) + p.K / 2, tag_in, wv[i] + 8, uw, live_in);
+              const uint4 a = make_uint4(xw[0], xw[1], xw[2], xw[3]);
+              const uint4 b = make_uint4(xw[4], xw[5], xw[6], xw[7]);
+              if constexpr (kSwiglu)
+                act16<true>(v, a, b, make_uint4(uw[0], uw[1], uw[2], uw[3]), make_uint4(uw[4], uw[5], uw[6], uw[7]));
+              else
+                act16<false>(v, a, b, a, b);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+            }
+            float sx;
+            const uint4 packed = quant16_octet(v, live, sx);
+            if (live) commit(m, r, kb, packed, sx);
+          }
         }
       } else {
         // The loads of kPasses passes are issued before any of them is
@@ -1375,6 +1438,8 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
                        p.prequant != 0))
     return 8;  // FP8GQ_ERR_UNSUPPORTED
   if (p.norm.norm && !pl.resident) return 8;
+  // tagged input words are read by the resident prologue only
+  if (p.gather.tagged && p.gather.wait_input && !pl.resident) return 8;
   auto fn = gemm_tm_kernel<MT, SW>;
   if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) != cudaSuccess) return 7;  // FP8GQ_ERR_LAUNCH
   if (csize > kTmMaxPortableCluster && ensure_nonportable_clusters(reinterpret_cast<const void*>(fn)) != cudaSuccess)
@@ -1514,6 +1579,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
                      const NormParams* norm = nullptr) {
   const int MT = tm_token_tile(M);
   if (N / kGroup > kTmMaxRowBlocks) return 8;  // FP8GQ_ERR_UNSUPPORTED
+  // tagged words: one launch per call (its sequence number tags every word)
+  if (gather && gather->tagged && M > MT) return 8;
   const size_t need = tm_workspace_bytes_for(M, N, K, sm_count);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255u))
     return 5;  // FP8GQ_ERR_WORKSPACE
@@ -1533,8 +1600,9 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
   if (grid_override > 0) {
     grid = grid_override < p.U ? grid_override : static_cast<int>(p.U);
   } else {
-    // the add + RMSNorm prologue needs the resident feed and room for its sums
-    const bool need_res = norm && norm->norm;
+    // the add + RMSNorm prologue needs the resident feed and room for its
+    // sums; tagged input words need the resident feed too
+    const bool need_res = (norm && norm->norm) || (gather && gather->tagged && gather->wait_input);
     const int mp = M < MT ? M : MT;
     const int64_t nb_bytes = need_res ? ((static_cast<int64_t>(mp) * (p.KB + 1) * 4 + 15) / 16) * 16 : 0;
     const int NBr = N / kGroup;
@@ -1640,6 +1708,8 @@ inline int launch_tm(bool swiglu, const void* x, int64_t ldx, const void* w, int
     CUtensorMap tmap_x;
     if (pre) {
       if (!cached_tmap(&tmap_x, 2, pre_xq + static_cast<int64_t>(m0) * K, p.M, K, K, MT)) return 7;
+    } else if (gather && gather->tagged && gather->wait_input) {
+      tmap_x = tmap_w;   // tagged words are not bf16 rows; the resident prologue reads them, no TMA
     } else if (!cached_tmap(&tmap_x, 1, xp, p.M, xcols, ldx, 0)) {
       return 7;
     }

@@ -140,8 +140,11 @@ gemv_row_kernel(const RowParams p) {
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
-  const int g0 = static_cast<int>((static_cast<int64_t>(blockIdx.x) * p.n_groups) / gridDim.x);
-  const int g1 = static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * p.n_groups) / gridDim.x);
+  // tagged words pair columns 2i, 2i + 1 in one store: with one row per group
+  // the CTAs split the rows in pairs (the host checks n_groups is even)
+  const int gu = (R == 1 && p.gather.tagged) ? 2 : 1;
+  const int g0 = gu * static_cast<int>((static_cast<int64_t>(blockIdx.x) * (p.n_groups / gu)) / gridDim.x);
+  const int g1 = gu * static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * (p.n_groups / gu)) / gridDim.x);
   const int n_my = g1 - g0;
 
   if (tid == 0) {
@@ -188,7 +191,14 @@ gemv_row_kernel(const RowParams p) {
   // the activation and the output belong to the stream's previous work
   grid_dependency_wait();
   bool in_ok = true;
-  if (p.gather.wait_input) {
+  // tagged words: the input carries this rank's last sequence number, the
+  // output the one after it
+  const bool tagged = p.gather.world > 0 && p.gather.tagged;
+  const unsigned int tag_in = tagged ? gather_seq_now(p.gather) : 0u;
+  const unsigned int tag_out = tag_after(tag_in);
+  const bool tagged_in = tagged && p.gather.wait_input;
+  bool tag_live = true;
+  if (p.gather.wait_input && !tagged) {
     // the activation is a gathered output: every rank's slice must be here
     if (warp == 0) {
       const bool w_ok = gather_wait_input(p.gather, lane);
@@ -250,18 +260,43 @@ gemv_row_kernel(const RowParams p) {
     float v[16];
     if (valid) {
       if constexpr (kSwiglu) {
-        const uint4* gp = reinterpret_cast<const uint4*>(p.x + 16 * c);
-        const uint4* up = reinterpret_cast<const uint4*>(p.x + p.K + 16 * c);
-        const uint4 g_a = gp[0], g_b = gp[1], u_a = up[0], u_b = up[1];
-        const uint32_t gw[8] = {g_a.x, g_a.y, g_a.z, g_a.w, g_b.x, g_b.y, g_b.z, g_b.w};
-        const uint32_t uw[8] = {u_a.x, u_a.y, u_a.z, u_a.w, u_b.x, u_b.y, u_b.z, u_b.w};
+        uint32_t gw[8], uw[8];
+        if (tagged_in) {
+          // word i of the row holds elements 2i, 2i + 1: gate at 8c, up at (K + 16c) / 2
+          const uint64_t* gp = reinterpret_cast<const uint64_t*>(p.x) + 8 * c;
+          const uint64_t* up = reinterpret_cast<const uint64_t*>(p.x) + p.K / 2 + 8 * c;
+          uint64_t gv[8], uv[8];
+          tagged_issue8(gp, gv);
+          tagged_issue8(up, uv);
+          tagged_finish8(gp, tag_in, gv, gw, tag_live);
+          tagged_finish8(up, tag_in, uv, uw, tag_live);
+        } else {
+          const uint4* gp = reinterpret_cast<const uint4*>(p.x + 16 * c);
+          const uint4* up = reinterpret_cast<const uint4*>(p.x + p.K + 16 * c);
+          const uint4 g_a = gp[0], g_b = gp[1], u_a = up[0], u_b = up[1];
+          gw[0] = g_a.x; gw[1] = g_a.y; gw[2] = g_a.z; gw[3] = g_a.w;
+          gw[4] = g_b.x; gw[5] = g_b.y; gw[6] = g_b.z; gw[7] = g_b.w;
+          uw[0] = u_a.x; uw[1] = u_a.y; uw[2] = u_a.z; uw[3] = u_a.w;
+          uw[4] = u_b.x; uw[5] = u_b.y; uw[6] = u_b.z; uw[7] = u_b.w;
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           v[2 * e] = silu_mul(bf16_lo(gw[e]), bf16_lo(uw[e]));
           v[2 * e + 1] = silu_mul(bf16_hi(gw[e]), bf16_hi(uw[e]));
         }
       } else {
-        if (p.norm.norm) {
+        if (tagged_in) {
+          const uint64_t* wp = reinterpret_cast<const uint64_t*>(p.x) + 8 * c;
+          uint64_t wv[8];
+          uint32_t xw[8];
+          tagged_issue8(wp, wv);
+          tagged_finish8(wp, tag_in, wv, xw, tag_live);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            v[2 * e] = bf16_lo(xw[e]);
+            v[2 * e + 1] = bf16_hi(xw[e]);
+          }
+        } else if (p.norm.norm) {
           const uint4* wp = reinterpret_cast<const uint4*>(p.norm.w + 16 * c);
           float sv[16];
           addn16(sv, p.x + 16 * c, p.norm.src_stride, p.norm.nsrc, p.norm.res + 16 * c);
@@ -366,7 +401,17 @@ gemv_row_kernel(const RowParams p) {
         }
         const int wrow0 = ((done_rows - 1) / kRowWindow) * kRowWindow;
         const int nrows = done_rows - wrow0;
-        if (lane < nrows) {
+        if (tagged) {
+          // rows come in pairs here (even row_begin, even row counts): the
+          // even lane stores rows lane, lane + 1 as one tagged word
+          float sum = 0.0f;
+          if (lane < nrows)
+            for (int w = 0; w < n_cwarps; ++w) sum += win[w * kRowWindow + lane];
+          const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(sum));
+          const uint32_t hi = __shfl_down_sync(0xffffffffu, lo, 1);
+          if (lane < nrows && !(lane & 1))
+            gather_store_pair(p.gather, 0, row_begin + wrow0 + lane, lo | (hi << 16), tag_out);
+        } else if (lane < nrows) {
           float sum = 0.0f;
           for (int w = 0; w < n_cwarps; ++w) sum += win[w * kRowWindow + lane];
           const __nv_bfloat16 v = __float2bfloat16_rn(sum);

@@ -41,7 +41,8 @@ class Gather(ctypes.Structure):
                 ("world", ctypes.c_int),
                 ("rank", ctypes.c_int),
                 ("wait_input", ctypes.c_int),
-                ("local_out", ctypes.c_int)]
+                ("local_out", ctypes.c_int),
+                ("tagged", ctypes.c_int)]
 
 
 class LaunchPlan(ctypes.Structure):
@@ -91,6 +92,7 @@ SIGNATURES = {
     "fp8gq_fused_gemv_quant_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
                                            _P, _SZ, _P]),
     "fp8gq_gather_wait": (_I, [ctypes.POINTER(Gather), _P]),
+    "fp8gq_gather_decode": (_I, [ctypes.POINTER(Gather), _I, _I, _P, _I64, _P]),
     "fp8gq_fused_swiglu_q_gemm_gather": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I, _I, ctypes.POINTER(Gather),
                                               _P, _SZ, _P]),
     "fp8gq_fused_reduce_add_rmsnorm_gemv_quant": (_I, [_P, _I, _I64, _I64, _P, _I64, _P, ctypes.c_float, _P, _I64,
@@ -121,6 +123,7 @@ SIGNATURES = {
                                                                ctypes.POINTER(Gather), _P, _SZ,
                                                                ctypes.POINTER(LaunchPlan)]),
     "fp8gq_prepare_gather_wait": (_I, [ctypes.POINTER(Gather), ctypes.POINTER(LaunchPlan)]),
+    "fp8gq_prepare_gather_decode": (_I, [ctypes.POINTER(Gather), _I, _I, _P, _I64, ctypes.POINTER(LaunchPlan)]),
     "fp8gq_launch_plans": (_I, [ctypes.POINTER(LaunchPlan), _I, _P]),
 }
 

@@ -97,6 +97,17 @@ def gathered_linear(x: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Ten
     return all_gather_columns(op(x, Wq_shard, Ws_shard), group=group)
 
 
+def untag(words: torch.Tensor) -> torch.Tensor:
+    """The bf16 values of tagged words [M, N/2] (int64) as [M, N] (a copy)."""
+    lo = words.contiguous().view(torch.int32)[..., 0::2].contiguous()
+    return lo.view(torch.bfloat16).reshape(*words.shape[:-1], 2 * words.shape[-1])
+
+
+def tags(words: torch.Tensor) -> torch.Tensor:
+    """The sequence numbers of tagged words [M, N/2] (int64), as int64."""
+    return (words >> 32) & 0xFFFFFFFF
+
+
 class PeerGather:
     """Gathered linears over peer memory (fp8gq_fused_gemv_quant_gather).
 
@@ -107,11 +118,22 @@ class PeerGather:
     [M, N] view into ``buffer`` -- on every rank at once.  Every rank must make
     the same sequence of ``linear`` calls.  ``wait()`` enqueues a wait for the
     last call's slices from every rank (before anything else reads ``out``).
+
+    ``tagged=True`` selects tagged words (the fp8gq_gather ``tagged`` field):
+    ``buffer`` is then int64, and an output [M, N] is a [M, N/2] view of it
+    whose word i holds columns 2i, 2i + 1 and the sequence number of the call
+    that wrote it.  No fence and no flag sits between a producer and its
+    consumer: a call with ``wait_input`` takes such a view as ``x`` -- the
+    output of the last call -- and its kernel polls the words it reads.
+    ``decode(out, dst)`` waits for a tagged output and writes it as bf16.
+    ``untag`` / ``tags`` read words on the host side.
     """
 
-    def __init__(self, buffer: torch.Tensor, group=None):
-        if buffer.dtype != torch.bfloat16 or not buffer.is_cuda or not buffer.is_contiguous():
-            raise TypeError("buffer must be a contiguous CUDA bf16 tensor")
+    def __init__(self, buffer: torch.Tensor, group=None, tagged: bool = False):
+        want = torch.int64 if tagged else torch.bfloat16
+        if buffer.dtype != want or not buffer.is_cuda or not buffer.is_contiguous():
+            raise TypeError(f"buffer must be a contiguous CUDA {str(want).split('.')[-1]} tensor")
+        self.tagged = bool(tagged)
         self.lib = _lib.load()
         self.group = group
         self.world = dist.get_world_size(group)
@@ -152,9 +174,12 @@ class PeerGather:
         return ptr.value
 
     def descriptor(self, out: torch.Tensor, col0: int, wait_input: bool) -> "_lib.Gather":
-        """The struct fp8gq_gather for output view ``out`` of ``buffer``."""
+        """The struct fp8gq_gather for output view ``out`` of ``buffer``
+        (tagged: a word view; ldo and col0 count elements, two per word)."""
+        es = out.element_size()
         off = out.data_ptr() - self.buffer.data_ptr()
-        if off < 0 or off + out.numel() * 2 > self.buffer.numel() * 2 or out.stride(1) != 1:
+        if (out.dtype != self.buffer.dtype or off < 0 or off + out.numel() * es > self.buffer.numel() * es
+                or out.stride(1) != 1):
             raise ValueError("out must be a row-major view into the PeerGather buffer")
         g = _lib.Gather()
         for r in range(self.world):
@@ -162,30 +187,69 @@ class PeerGather:
             g.flags[r] = self.flag_ptrs[r]
         g.counter = self.state.data_ptr()
         g.seq = self.state.data_ptr() + 4
-        g.ldo = out.stride(0)
+        g.ldo = out.stride(0) * (2 if self.tagged else 1)
         g.col0 = col0
         g.world = self.world
         g.rank = self.rank
         g.wait_input = 1 if wait_input else 0
+        g.tagged = 1 if self.tagged else 0
         return g
+
+    def _cols(self, out: torch.Tensor) -> int:
+        """Columns (elements) of an output view."""
+        return out.shape[1] * (2 if self.tagged else 1)
+
+    def _x_args(self, x: torch.Tensor, wait_input: bool):
+        """(pointer, row stride in elements, K) of an input: tagged words when
+        a tagged call waits for it, bf16 otherwise."""
+        if self.tagged and wait_input:
+            if x.dtype != torch.int64 or x.dim() != 2 or x.stride(1) != 1:
+                raise TypeError("a tagged call that waits for its input takes a 2-D int64 word view")
+            return x.data_ptr(), 2 * x.stride(0), 2 * x.shape[1]
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(1) != 1:
+            raise TypeError("x must be a 2-D bf16 tensor, contiguous along K")
+        return x.data_ptr(), x.stride(0), x.shape[1]
 
     def linear(self, x: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Tensor, out: torch.Tensor,
                wait_input: bool = True, desc=None):
         """out[:, rank*Nr:(rank+1)*Nr] = fused_gemv_quant(x, Wq_shard, Ws_shard) on every rank."""
-        M, K = x.shape
+        return self._gathered(False, x, Wq_shard, Ws_shard, out, wait_input, desc)
+
+    def swiglu_linear(self, gu: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Tensor, out: torch.Tensor,
+                      wait_input: bool = True, desc=None):
+        """out[:, rank*Nr:(rank+1)*Nr] = fused_swiglu_q_gemm(gu, Wq_shard, Ws_shard) on every rank
+        (gu the full [gate | up] row, e.g. a gathered gate_up output)."""
+        return self._gathered(True, gu, Wq_shard, Ws_shard, out, wait_input, desc)
+
+    def _gathered(self, swiglu, x, Wq_shard, Ws_shard, out, wait_input, desc, plan=None):
+        wait_input = bool(desc.wait_input) if desc is not None else wait_input
+        xp, ldx, cols = self._x_args(x, wait_input)
+        M = x.shape[0]
+        if swiglu and cols % 2:
+            raise ops.ShapeError("gu must hold [gate | up]: an even number of columns")
+        K = cols // 2 if swiglu else cols
         Nr, ldw, ldws = ops._check_weight_strides(Wq_shard, Ws_shard, K)
-        if out.shape != (M, Nr * self.world):
-            raise ops.ShapeError(f"out must be [{M}, {Nr * self.world}], got {tuple(out.shape)}")
+        if out.shape[0] != M or self._cols(out) != Nr * self.world:
+            raise ops.ShapeError(f"out must hold [{M}, {Nr * self.world}], got {tuple(out.shape)}")
         g = desc if desc is not None else self.descriptor(out, self.rank * Nr, wait_input)
         dev = x.device
         stream = ops._stream(dev)
         nbytes = ops._workspace_bytes(self.lib, dev, M, Nr, K)
-        ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, stream)[1:] if nbytes else (None, 0)
-        st = self.lib.fp8gq_fused_gemv_quant_gather(
-            x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), ldw, Ws_shard.data_ptr(), ldws, M, Nr, K,
-            ctypes.byref(g), ws_ptr, ws_n, stream)
-        _lib.check(st, "fp8gq_fused_gemv_quant_gather")
-        return out
+        buf, ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, stream) if nbytes else (None, None, 0)
+        base = "fused_swiglu_q_gemm_gather" if swiglu else "fused_gemv_quant_gather"
+        if plan is None:
+            name = "fp8gq_" + base
+            st = getattr(self.lib, name)(xp, ldx, Wq_shard.data_ptr(), ldw, Ws_shard.data_ptr(), ldws, M, Nr, K,
+                                         ctypes.byref(g), ws_ptr, ws_n, stream)
+            _lib.check(st, name)
+            return out
+        from .prepared import Plan
+        name = "fp8gq_prepare_" + base
+        pl = Plan(name, (x, Wq_shard, Ws_shard, out, buf, g), out)
+        st = getattr(self.lib, name)(xp, ldx, Wq_shard.data_ptr(), ldw, Ws_shard.data_ptr(), ldws, M, Nr, K,
+                                     ctypes.byref(g), ws_ptr, ws_n, ctypes.byref(pl.cplan))
+        _lib.check(st, name)
+        return pl
 
     def partial_descriptor(self, slabs: torch.Tensor) -> "_lib.Gather":
         """The struct fp8gq_gather that stores this rank's [M, N] partial into
@@ -253,21 +317,12 @@ class PeerGather:
     def prepare_linear(self, x: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Tensor, out: torch.Tensor,
                        wait_input: bool = True, desc=None):
         """The plan of ``linear(x, Wq_shard, Ws_shard, out, wait_input)``."""
-        from .prepared import Plan
-        M, K = x.shape
-        Nr, ldw, ldws = ops._check_weight_strides(Wq_shard, Ws_shard, K)
-        if out.shape != (M, Nr * self.world):
-            raise ops.ShapeError(f"out must be [{M}, {Nr * self.world}], got {tuple(out.shape)}")
-        g = desc if desc is not None else self.descriptor(out, self.rank * Nr, wait_input)
-        dev = x.device
-        nbytes = ops._workspace_bytes(self.lib, dev, M, Nr, K)
-        buf, ws_ptr, ws_n = ops._workspace_entry(dev, nbytes, ops._stream(dev)) if nbytes else (None, None, 0)
-        plan = Plan("fp8gq_prepare_fused_gemv_quant_gather", (x, Wq_shard, Ws_shard, out, buf, g), out)
-        st = self.lib.fp8gq_prepare_fused_gemv_quant_gather(
-            x.data_ptr(), x.stride(0), Wq_shard.data_ptr(), ldw, Ws_shard.data_ptr(), ldws, M, Nr, K,
-            ctypes.byref(g), ws_ptr, ws_n, ctypes.byref(plan.cplan))
-        _lib.check(st, plan.what)
-        return plan
+        return self._gathered(False, x, Wq_shard, Ws_shard, out, wait_input, desc, plan=True)
+
+    def prepare_swiglu_linear(self, gu: torch.Tensor, Wq_shard: torch.Tensor, Ws_shard: torch.Tensor,
+                              out: torch.Tensor, wait_input: bool = True, desc=None):
+        """The plan of ``swiglu_linear(gu, Wq_shard, Ws_shard, out, wait_input)``."""
+        return self._gathered(True, gu, Wq_shard, Ws_shard, out, wait_input, desc, plan=True)
 
     def prepare_linear_partial(self, x: torch.Tensor, Wq_cols: torch.Tensor, Ws_cols: torch.Tensor,
                                slabs: torch.Tensor, swiglu: bool = False, desc=None):
@@ -316,9 +371,39 @@ class PeerGather:
         _lib.check(st, name)
         return plan
 
+    def decode(self, out: torch.Tensor, dst: torch.Tensor | None = None) -> torch.Tensor:
+        """Tagged words: enqueue a kernel that waits until every word of the
+        full output ``out`` (a word view, the last call's output) has arrived
+        and writes its values into ``dst`` (bf16 [M, N], made if None)."""
+        g, dst, M, N = self._decode_args(out, dst)
+        _lib.check(self.lib.fp8gq_gather_decode(ctypes.byref(g), M, N, dst.data_ptr(), dst.stride(0),
+                                                ops._stream(out.device)), "fp8gq_gather_decode")
+        return dst
+
+    def prepare_decode(self, out: torch.Tensor, dst: torch.Tensor | None = None):
+        """The plan of ``decode(out, dst)``; ``plan.out`` is ``dst``."""
+        from .prepared import Plan
+        g, dst, M, N = self._decode_args(out, dst)
+        plan = Plan("fp8gq_prepare_gather_decode", (out, dst, g), dst)
+        _lib.check(self.lib.fp8gq_prepare_gather_decode(ctypes.byref(g), M, N, dst.data_ptr(), dst.stride(0),
+                                                        ctypes.byref(plan.cplan)), plan.what)
+        return plan
+
+    def _decode_args(self, out, dst):
+        if not self.tagged:
+            raise ValueError("decode is for tagged words; use wait() with flags")
+        M, N = out.shape[0], self._cols(out)
+        if dst is None:
+            dst = torch.empty(M, N, dtype=torch.bfloat16, device=out.device)
+        if dst.dtype != torch.bfloat16 or tuple(dst.shape) != (M, N) or dst.stride(1) != 1:
+            raise ops.ShapeError(f"dst must be a bf16 [{M}, {N}] tensor, contiguous along its rows")
+        return self.descriptor(out, 0, True), dst, M, N
+
     def prepare_wait(self, out: torch.Tensor):
         """The plan of ``wait(out)``."""
         from .prepared import Plan
+        if self.tagged:
+            raise ValueError("tagged words are waited for by prepare_decode(out, dst)")
         g = self.descriptor(out, 0, True)
         plan = Plan("fp8gq_prepare_gather_wait", (out, g), out)
         _lib.check(self.lib.fp8gq_prepare_gather_wait(ctypes.byref(g), ctypes.byref(plan.cplan)), plan.what)
@@ -326,6 +411,8 @@ class PeerGather:
 
     def wait(self, out: torch.Tensor):
         """Enqueue a wait for the last gathered call's slices from every rank."""
+        if self.tagged:
+            raise ValueError("tagged words are waited for by decode(out, dst)")
         g = self.descriptor(out, 0, True)
         _lib.check(self.lib.fp8gq_gather_wait(ctypes.byref(g), ops._stream(out.device)), "fp8gq_gather_wait")
 

@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version_and_status_strings(lib):
-    assert lib.fp8gq_version() == 1
+    assert lib.fp8gq_version() == 2
     for code in range(0, 11):
         assert lib.fp8gq_status_string(code)
     assert b"unknown" in lib.fp8gq_status_string(1234)

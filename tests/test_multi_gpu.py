@@ -17,6 +17,12 @@ their output slices into every rank's buffer over NVLink (fp8gq.dist.PeerGather)
 * Paired tensor parallelism: row-parallel partials stored into every rank's
   slab, summed by the next column-parallel linear's reduce + add + RMSNorm
   prologue; each stage against the oracle.
+* The same chains with tagged words (PeerGather(tagged=True)): each linear
+  reads the previous one's tagged output directly, the last stage of each
+  chain a SwiGLU over a gathered [gate | up] output; every stage decoded on
+  every rank against the oracle and across ranks, the back-to-back reruns
+  with one rank held back, and every word of the final output carrying the
+  sequence number of the call that wrote it.
 """
 import os
 import socket
@@ -35,6 +41,13 @@ WORLDS = [2, 4, 8]
 # long-K linear (12288 -> 4096); M = 4 runs the tile kernel.
 CHAINS = [(1, [4096, 6144, 4096, 4096, 12288, 4096, 4096]), (4, [2048, 3072, 2048, 2048])]
 SKEW_CYCLES = 400_000      # ~0.2 ms sleep kernel that pushes one rank behind
+# tagged chains (M, stages): stage (K, N, swiglu) maps an input of K columns
+# (2K for a SwiGLU stage, which reads the previous [gate | up] output) to N.
+# At M = 1 the shards span the row kernel (one, two and four rows per group)
+# and the tile kernel; M = 4 runs the tile kernel.
+TAGGED_CHAINS = [(1, [(4096, 6144, False), (6144, 4096, False), (4096, 12288, False), (12288, 4096, False),
+                      (4096, 6144, False), (3072, 4096, True)]),
+                 (4, [(2048, 3072, False), (3072, 2048, False), (2048, 2048, False), (1024, 2048, True)])]
 
 
 def _free_port():
@@ -206,6 +219,80 @@ def _skip_unless(world):
 def test_gathered_chain_matches_oracle(world):
     _skip_unless(world)
     _spawn(_chain_worker, world)
+
+
+def _tagged_chain_worker(rank, world, port, result_q):
+    dev = _setup(rank, world, port)
+    import torch.distributed as dist
+
+    import fp8gq
+    from fp8gq import dist as fdist
+    errs = []
+    try:
+        fp8gq.load()
+        for ci, (M, stages) in enumerate(TAGGED_CHAINS):
+            n = len(stages)
+            wmax = max(N for _, N, _ in stages)
+            words = torch.zeros(M * wmax + 32, dtype=torch.int64, device=dev)   # two buffers of M * wmax / 2
+            pg = fdist.PeerGather(words, tagged=True)
+            bufs = [words[:M * wmax // 2], words[M * wmax // 2:M * wmax]]
+            lins = []
+            for j, (K, N, sw) in enumerate(stages):
+                wq, ws = _weight(N, K, 5000 + 100 * ci + j, dev)
+                lins.append((wq, ws) + fdist.shard_rows(wq, ws, rank, world))
+            x0 = _activation(M, stages[0][0], 91 + ci, dev)
+
+            def out_of(j):
+                N = stages[j][1]
+                return bufs[j % 2].view(-1)[:M * N // 2].view(M, N // 2)
+
+            def run(snapshots=None, skew_at=None):
+                for j, (K, N, sw) in enumerate(stages):
+                    if skew_at is not None and rank == skew_at(j):
+                        torch.cuda._sleep(SKEW_CYCLES)
+                    x = x0 if j == 0 else out_of(j - 1)
+                    call = pg.swiglu_linear if sw else pg.linear
+                    call(x, lins[j][2], lins[j][3], out_of(j), wait_input=j > 0)
+                    if snapshots is not None:
+                        snapshots.append(pg.decode(out_of(j)))
+
+            snaps = []
+            run(snaps, skew_at=lambda j: j % world)
+            torch.cuda.synchronize()
+            for j in range(n):
+                _same_on_every_rank(errs, f"tagged chain {ci} M={M} stage {j}", snaps[j])
+            if rank == 0:
+                for j, (K, N, sw) in enumerate(stages):
+                    x = x0 if j == 0 else snaps[j - 1]
+                    _oracle_check(errs, f"tagged chain {ci} M={M} stage {j} ({'swiglu ' if sw else ''}{K}->{N})",
+                                  snaps[j], x, lins[j][0], lins[j][1], swiglu=sw)
+            dist.barrier()
+            run(skew_at=lambda j: world - 1 if j == n - 1 else None)
+            run(skew_at=lambda j: world - 1 if j == n - 1 else None)
+            final = pg.decode(out_of(n - 1))
+            torch.cuda.synchronize()
+            if not torch.equal(final, snaps[n - 1]):
+                errs.append(f"tagged chain {ci} M={M}: back-to-back rerun changed the final output in "
+                            f"{(final != snaps[n - 1]).sum().item()} elements")
+            tg = fdist.tags(out_of(n - 1))
+            if not bool((tg == 3 * n).all()):
+                errs.append(f"tagged chain {ci} M={M}: final words tagged {sorted(set(tg.flatten().tolist()))}, "
+                            f"expected {3 * n}")
+            if fp8gq.device_error() != 0:
+                errs.append(f"device error word {fp8gq.device_error():#x}")
+            pg.close()
+        result_q.put((rank, errs))
+    except Exception as e:
+        result_q.put((rank, errs + [f"exception: {e!r}"]))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_tagged_chain_matches_oracle(world):
+    _skip_unless(world)
+    _spawn(_tagged_chain_worker, world)
 
 
 def _paired_worker(rank, world, port, result_q):
