@@ -123,6 +123,70 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
+# ------------------------------------------------------------- NVLink --
+class NvlinkCounter:
+    """This GPU's NVLink traffic over a window, from the GPU performance
+    monitor (NVML GPM samples before and after; read-only, nothing on the GPU
+    is changed): total transmitted and received bytes per second over all
+    links, times the window.  `error` holds the reason when the counters are
+    not available (no GPM support, no pynvml)."""
+
+    def __init__(self, dev_index: int):
+        self.error = None
+        self.nv = None
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = nv.nvmlDeviceGetHandleByIndex(dev_index)
+            sup = nv.nvmlGpmQueryDeviceSupport(self.h)
+            if not sup.isSupportedDevice:
+                self.error = "GPM not supported on this device"
+            else:
+                self.s = [nv.nvmlGpmSampleAlloc(), nv.nvmlGpmSampleAlloc()]
+        except Exception as e:          # counters are optional evidence
+            self.error = f"{type(e).__name__}: {e}"
+
+    def start(self):
+        if self.error is None:
+            try:
+                self.nv.nvmlGpmSampleGet(self.h, self.s[0])
+                self.t0 = time.monotonic()
+            except Exception as e:
+                self.error = f"{type(e).__name__}: {e}"
+
+    def stop(self):
+        """(tx bytes, rx bytes) over the window, or None."""
+        if self.error is not None:
+            return None
+        try:
+            nv = self.nv
+            nv.nvmlGpmSampleGet(self.h, self.s[1])
+            dt = time.monotonic() - self.t0
+            mg = nv.c_nvmlGpmMetricsGet_t()
+            mg.version = nv.NVML_GPM_METRICS_GET_VERSION
+            mg.numMetrics = 2
+            mg.sample1 = self.s[0]
+            mg.sample2 = self.s[1]
+            mg.metrics[0].metricId = nv.NVML_GPM_METRIC_NVLINK_TOTAL_TX_PER_SEC
+            mg.metrics[1].metricId = nv.NVML_GPM_METRIC_NVLINK_TOTAL_RX_PER_SEC
+            nv.nvmlGpmMetricsGet(mg)
+            # the GPM rates are in MiB/s
+            return (mg.metrics[0].value * 2**20 * dt, mg.metrics[1].value * 2**20 * dt, dt)
+        except Exception as e:
+            self.error = f"{type(e).__name__}: {e}"
+            return None
+
+    def close(self):
+        if self.nv is not None:
+            try:
+                for smp in getattr(self, "s", []):
+                    self.nv.nvmlGpmSampleFree(smp)
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
+
+
 # ------------------------------------------------------------- clocks --
 class ClockSampler:
     """nvidia-smi samples of the job's GPUs (every rank's, identified by UUID),
@@ -730,10 +794,13 @@ def run_ours(args):
     # ---- timed region: K steps (graph replays), CUDA events, max over ranks
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(uuids, active=rank == 0)
+    nvc = NvlinkCounter(local) if world > 1 else None
     with sampler:
         barrier()
         torch.cuda.synchronize()
         sampler.mark()
+        if nvc is not None:
+            nvc.start()
         for _ in range(n_pre):
             graph.replay()
         start.record()
@@ -743,6 +810,7 @@ def run_ours(args):
         for _ in range(n_post):
             graph.replay()
         torch.cuda.synchronize()
+        nv_win = nvc.stop() if nvc is not None else None
         sampler.mark()
         barrier()
     ms = start.elapsed_time(end) / args.steps
@@ -751,6 +819,27 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     clocks = sampler.summary()
+    nvlink = None
+    if world > 1:
+        # NVLink bytes per step, each rank's own counters over the loaded
+        # window (every replay in it is the same step), against what the step
+        # must send: each rank's output slices (or partials) to world - 1 peers
+        n_win = n_pre + args.steps + n_post
+        mine = [nv_win[0] / n_win, nv_win[1] / n_win] if nv_win is not None else [-1.0, -1.0]
+        allv = [None] * world
+        dist.all_gather_object(allv, (mine, nvc.error))
+        nvc.close()
+        if paired:
+            alg = 2 * LAYERS * SHAPES[0][1] * 2 * (world - 1)
+        elif pg is not None:
+            alg = LAYERS * sum(N // world for _, _, N in SHAPES) * (4 if tagged else 2) * (world - 1)
+        else:
+            alg = None
+        nvlink = {"tx_bytes_per_step": [round(v[0][0]) if v[0][0] >= 0 else None for v in allv],
+                  "rx_bytes_per_step": [round(v[0][1]) if v[0][1] >= 0 else None for v in allv],
+                  "algorithmic_tx_bytes_per_step": alg,
+                  "source": "NVML GPM NVLINK_TOTAL_TX/RX_PER_SEC over the loaded window, per rank",
+                  "errors": [v[1] for v in allv if v[1]] or None}
     value = STEP_BYTES / (ms * 1e-3) / 1e9
     launches = (LAYERS * len(SHAPES) + (1 if pg is not None else 0)) * args.steps
 
@@ -924,7 +1013,7 @@ def run_ours(args):
             ms_ = float(t.item())
         return ms_
 
-    def e2e_pipelined_ms():
+    def e2e_pipelined_ms(graphs=False):
         """The prepared step with the copies overlapped, through two copies of
         the step's buffers: step k runs on copy k % 2, its inputs are copied in
         (one stream) while step k - 1 runs, and its outputs copied out (another
@@ -933,15 +1022,28 @@ def run_ours(args):
         the copy out of step k - 1 (same copy as step k + 1), which is also the
         point after which the other ranks may store step k + 1's slices into
         it -- so the chain of launches is not broken at every layer.  Every
-        step's copies, in and out, are inside the timed region."""
+        step's copies, in and out, are inside the timed region.  With graphs,
+        each half of the step (its launch lists as they are) is captured once
+        into a CUDA graph and replayed, as a serving loop replays its decode
+        step: eager launches cost the device more per launch than replayed
+        ones."""
         if paired or prepared is None:
             return None
         npl = len(SHAPES)
         lists = []
         for parity in (0, 1):
             full = prepared if parity == 0 else prepared_step_list(1)
-            lists.append((fp8gq.LaunchList(full.plans[:npl * (LAYERS - 1)]),
-                          fp8gq.LaunchList(full.plans[npl * (LAYERS - 1):])))
+            head = fp8gq.LaunchList(full.plans[:npl * (LAYERS - 1)])
+            tail = fp8gq.LaunchList(full.plans[npl * (LAYERS - 1):])
+            if graphs:
+                gh, gt = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gh):
+                    head.run()
+                with torch.cuda.graph(gt):
+                    tail.run()
+                lists.append((gh, gt))
+            else:
+                lists.append((head, tail))
         comp = torch.cuda.current_stream(dev)
         s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
         in_ready = [torch.cuda.Event(), torch.cuda.Event()]
@@ -961,10 +1063,10 @@ def run_ours(args):
                 in_ready[q].record(s_in)
             comp.wait_event(in_ready[q])
             head, tail = lists[q]
-            head.run()
+            head.replay() if graphs else head.run()
             if k >= 1:
                 comp.wait_event(out_free[(k - 1) % 2])   # step k - 1's outputs are copied out
-            tail.run()
+            tail.replay() if graphs else tail.run()
             step_done[q].record(comp)
             with torch.cuda.stream(s_out):
                 s_out.wait_event(step_done[q])
@@ -993,7 +1095,8 @@ def run_ours(args):
 
     eager_ms = e2e_ms_of(step)
     serial_ms = e2e_ms_of(prepared.run) if prepared is not None else eager_ms
-    piped_ms = e2e_pipelined_ms()
+    piped_eager_ms = e2e_pipelined_ms()
+    piped_ms = e2e_pipelined_ms(graphs=True)
     e2e_ms = piped_ms if piped_ms is not None else serial_ms
     # where the end-to-end time goes: the same loop without the copies, and
     # the copies alone
@@ -1009,10 +1112,14 @@ def run_ours(args):
                                                           "PeerGather.prepare_linear calls" if pg is not None else
                                                           "fp8gq.prepare_fused_gemv_quant calls") +
                      (", two copies of the step's buffers: each step's inputs copied in while the step before "
-                      "runs and its outputs copied out while the step after runs, on two copy streams (eager, "
-                      "no graph)" if piped_ms is not None else
+                      "runs and its outputs copied out while the step after runs, on two copy streams; each half "
+                      "of the step captured once into a CUDA graph and replayed" if piped_ms is not None else
                       ", one run per step, copies before and after it (eager, no graph)"))
                     if prepared is not None else "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
+           "eager_pipelined": ({"ms_per_step": round(piped_eager_ms, 4),
+                                "value": round(STEP_BYTES / (piped_eager_ms * 1e-3) / 1e9, 3),
+                                "path": "the same pipelined loop with the launch lists issued eagerly (no graph)"}
+                               if piped_eager_ms is not None else None),
            "serial_copies": {"ms_per_step": round(serial_ms, 4),
                              "value": round(STEP_BYTES / (serial_ms * 1e-3) / 1e9, 3)},
            "prepared_matches_calls": prepared_same,
@@ -1058,7 +1165,7 @@ def run_ours(args):
                            "static_weights": bool(args.static_weights)},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
                 "per_linear": per, "per_linear_row_kernel": per_row, "per_linear_tile_kernel": per_tm, **extra,
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "parity": parity,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "parity": parity, "nvlink": nvlink,
                 "gpu_launches": launches, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:

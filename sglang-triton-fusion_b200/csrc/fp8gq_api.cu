@@ -97,23 +97,24 @@ inline int launch_status() {
 // ----------------------------------------------------------------- row --
 using RowKernel = void (*)(const RowParams);
 
-template <int C, int R, bool S>
+template <int C, int R, bool S, bool T>
 RowKernel row_fn() {
-  return gemv_row_kernel<C, R, S>;
+  return gemv_row_kernel<C, R, S, T>;
 }
 
 constexpr int kRowCs[] = {1, 2, 3, 4, 6, 8};
 constexpr int kRowRs[] = {1, 2, 4};
 
-template <bool S>
+// S: SwiGLU input; T: tagged-word gather
+template <bool S, bool T = false>
 RowKernel row_lookup(int ci, int ri) {
   static const RowKernel table[6][3] = {
-      {row_fn<1, 1, S>(), row_fn<1, 2, S>(), row_fn<1, 4, S>()},
-      {row_fn<2, 1, S>(), row_fn<2, 2, S>(), row_fn<2, 4, S>()},
-      {row_fn<3, 1, S>(), row_fn<3, 2, S>(), row_fn<3, 4, S>()},
-      {row_fn<4, 1, S>(), row_fn<4, 2, S>(), row_fn<4, 4, S>()},
-      {row_fn<6, 1, S>(), row_fn<6, 2, S>(), row_fn<6, 4, S>()},
-      {row_fn<8, 1, S>(), row_fn<8, 2, S>(), row_fn<8, 4, S>()},
+      {row_fn<1, 1, S, T>(), row_fn<1, 2, S, T>(), row_fn<1, 4, S, T>()},
+      {row_fn<2, 1, S, T>(), row_fn<2, 2, S, T>(), row_fn<2, 4, S, T>()},
+      {row_fn<3, 1, S, T>(), row_fn<3, 2, S, T>(), row_fn<3, 4, S, T>()},
+      {row_fn<4, 1, S, T>(), row_fn<4, 2, S, T>(), row_fn<4, 4, S, T>()},
+      {row_fn<6, 1, S, T>(), row_fn<6, 2, S, T>(), row_fn<6, 4, S, T>()},
+      {row_fn<8, 1, S, T>(), row_fn<8, 2, S, T>(), row_fn<8, 4, S, T>()},
   };
   return table[ci][ri];
 }
@@ -183,7 +184,9 @@ int launch_row(bool swiglu, const void* x, const void* w, int64_t ldw, const flo
     const int Tj = ((n_chunks + Cj - 1) / Cj + 31) / 32 * 32;
     const size_t sj = row_smem_bytes(stages, stage_bytes, Tj / 32);
     if (sj > static_cast<size_t>(di.max_smem_optin)) continue;
-    RowKernel fj = swiglu ? row_lookup<true>(cj, ri) : row_lookup<false>(cj, ri);
+    const bool tg = gather && gather->world > 0 && gather->tagged;
+    RowKernel fj = swiglu ? (tg ? row_lookup<true, true>(cj, ri) : row_lookup<true>(cj, ri))
+                          : (tg ? row_lookup<false, true>(cj, ri) : row_lookup<false>(cj, ri));
     if (ensure_max_smem(reinterpret_cast<const void*>(fj), di.max_smem_optin) != cudaSuccess) return FP8GQ_ERR_LAUNCH;
     const int pj = row_ctas_per_sm(fj, Tj + 32, sj);
     if (pj < 1) continue;

@@ -384,7 +384,9 @@ __device__ __forceinline__ int tile_pos(int j, int kb0, int KB, int kpb) {
 }
 
 // ------------------------------------------------------------- kernel --
-template <int MT, bool kSwiglu>
+// kTagged: the gather uses tagged words (a separate instance, so that the
+// plain kernel's code is unchanged by the protocol).
+template <int MT, bool kSwiglu, bool kTagged = false>
 __global__ void __launch_bounds__(kTmThreads, tm_ctas_per_sm<MT>())
 gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                const TmParams p) {
@@ -441,14 +443,14 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   const int kb0 = static_cast<int>(u0 - static_cast<int64_t>(nb0) * p.KB);
   // tagged words: the input carries this rank's last sequence number, the
   // output the one after it (read after the grid-dependency wait)
-  const bool tagged = p.gather.world > 0 && p.gather.tagged;
+  constexpr bool tagged = kTagged;
   const bool tagged_in = tagged && p.gather.wait_input;
   unsigned int tag_in = 0u, tag_out = 0u;
   // output element (token m, column n of this launch): local, or to every
   // rank (tagged: all 32 lanes together, consecutive columns on consecutive
   // lanes -- true of every call below)
   auto store_out = [&](int m, int n, __nv_bfloat16 v) {
-    if (tagged)
+    if constexpr (kTagged)
       gather_store_tagged(p.gather, m, n, v, tag_out);
     else if (gather_publishes(p.gather))
       gather_store(p.gather, m, n, v);
@@ -522,7 +524,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   }
   grid_dependency_wait();
-  if (tagged) {
+  if constexpr (kTagged) {
     tag_in = gather_seq_now(p.gather);
     tag_out = tag_after(tag_in);
   }
@@ -1440,10 +1442,6 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   if (p.norm.norm && !pl.resident) return 8;
   // tagged input words are read by the resident prologue only
   if (p.gather.tagged && p.gather.wait_input && !pl.resident) return 8;
-  auto fn = gemm_tm_kernel<MT, SW>;
-  if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) != cudaSuccess) return 7;  // FP8GQ_ERR_LAUNCH
-  if (csize > kTmMaxPortableCluster && ensure_nonportable_clusters(reinterpret_cast<const void*>(fn)) != cudaSuccess)
-    return 7;
   p.stages = pl.stages;
   p.npw = pl.npw;
   p.resident = pl.resident;
@@ -1451,9 +1449,22 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   p.x_off = pl.x_off;
   p.bar_off = pl.bar_off;
   p.csize = csize;
-  if (launch_with_pdl_cluster(fn, dim3(grid), dim3(kTmThreads), pl.smem, stream, csize, tw, tx, p) != cudaSuccess)
-    return 7;
-  return cudaGetLastError() == cudaSuccess ? 0 : 7;
+  auto go = [&](auto fn) -> int {
+    if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) != cudaSuccess) return 7;  // FP8GQ_ERR_LAUNCH
+    if (csize > kTmMaxPortableCluster && ensure_nonportable_clusters(reinterpret_cast<const void*>(fn)) != cudaSuccess)
+      return 7;
+    if (launch_with_pdl_cluster(fn, dim3(grid), dim3(kTmThreads), pl.smem, stream, csize, tw, tx, p) != cudaSuccess)
+      return 7;
+    return cudaGetLastError() == cudaSuccess ? 0 : 7;
+  };
+  if (p.gather.world > 0 && p.gather.tagged) {
+    // tagged words: calls of at most 16 tokens, the 16-token tile only
+    if constexpr (MT == 16)
+      return go(gemm_tm_kernel<16, SW, true>);
+    else
+      return 8;
+  }
+  return go(gemm_tm_kernel<MT, SW, false>);
 }
 
 // How many clusters of `csize` CTAs with `smem` bytes each can be resident at

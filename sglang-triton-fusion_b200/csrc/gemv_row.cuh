@@ -125,7 +125,9 @@ __device__ __forceinline__ int row_of_lane(int lane) {
   return row;
 }
 
-template <int C, int R, bool kSwiglu>
+// kTagged: the gather uses tagged words (a separate instance, so that the
+// plain kernel's code is unchanged by the protocol).
+template <int C, int R, bool kSwiglu, bool kTagged = false>
 __global__ void __launch_bounds__(kRowMaxConsumerThreads + 32, 1)
 gemv_row_kernel(const RowParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -142,7 +144,7 @@ gemv_row_kernel(const RowParams p) {
 
   // tagged words pair columns 2i, 2i + 1 in one store: with one row per group
   // the CTAs split the rows in pairs (the host checks n_groups is even)
-  const int gu = (R == 1 && p.gather.tagged) ? 2 : 1;
+  constexpr int gu = (R == 1 && kTagged) ? 2 : 1;
   const int g0 = gu * static_cast<int>((static_cast<int64_t>(blockIdx.x) * (p.n_groups / gu)) / gridDim.x);
   const int g1 = gu * static_cast<int>((static_cast<int64_t>(blockIdx.x + 1) * (p.n_groups / gu)) / gridDim.x);
   const int n_my = g1 - g0;
@@ -193,7 +195,7 @@ gemv_row_kernel(const RowParams p) {
   bool in_ok = true;
   // tagged words: the input carries this rank's last sequence number, the
   // output the one after it
-  const bool tagged = p.gather.world > 0 && p.gather.tagged;
+  constexpr bool tagged = kTagged;
   const unsigned int tag_in = tagged ? gather_seq_now(p.gather) : 0u;
   const unsigned int tag_out = tag_after(tag_in);
   const bool tagged_in = tagged && p.gather.wait_input;
@@ -401,7 +403,7 @@ gemv_row_kernel(const RowParams p) {
         }
         const int wrow0 = ((done_rows - 1) / kRowWindow) * kRowWindow;
         const int nrows = done_rows - wrow0;
-        if (tagged) {
+        if constexpr (kTagged) {
           // rows come in pairs here (even row_begin, even row counts): the
           // even lane stores rows lane, lane + 1 as one tagged word
           float sum = 0.0f;
