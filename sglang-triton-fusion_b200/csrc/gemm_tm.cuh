@@ -79,6 +79,7 @@ constexpr size_t kTmSmemReservedPerCta = 1024;   // what the runtime keeps per r
 
 constexpr int kTmMaxStages = 8;     // ring depth limit (barrier arrays are sized for it)
 constexpr int kTmMaxCluster = 16;   // largest split-K cluster (16: B200's non-portable size)
+constexpr int64_t kTmPushMaxBytes = 16 * 1024;   // largest receive area of a split-K reduction by push
 constexpr int kTmMaxPortableCluster = 8;   // clusters above this need the non-portable attribute
 
 // CTAs per SM the 16-token tile may run at (two MMA issue streams and two
@@ -112,6 +113,8 @@ struct TmParams {
   int prequant;             // pre-quantised feed: B tiles by TMA from xq (tmap_x), scales from sx_pre
   const float* sx_pre;      // [M, K/128] scales of the pre-quantised activation
   int csize;                // split-K cluster size (1: none; the CTAs of a row block form a cluster)
+  int red_push;             // cluster split-K by push: the other CTAs copy their partials to rank 0
+  uint32_t red_off;         // push: rank 0's receive area [csize - 1][M][128] fp32 (bytes from the base)
   int early_weights;        // weights and block scales are static: load them before the grid-dependency wait
   int* counters;            // [kTmMaxRowBlocks], zero on entry and exit
   float* partials;          // [G][2][MT][128]
@@ -384,9 +387,10 @@ __device__ __forceinline__ int tile_pos(int j, int kb0, int KB, int kpb) {
 }
 
 // ------------------------------------------------------------- kernel --
-// kTagged: the gather uses tagged words (a separate instance, so that the
-// plain kernel's code is unchanged by the protocol).
-template <int MT, bool kSwiglu, bool kTagged = false>
+// kTagged: the gather uses tagged words; kCluster: a cluster split-K launch
+// (csize > 1).  Separate instances, so that each kernel carries only the code
+// of its own protocol and reduction.
+template <int MT, bool kSwiglu, bool kTagged = false, bool kCluster = false>
 __global__ void __launch_bounds__(kTmThreads, tm_ctas_per_sm<MT>())
 gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                const TmParams p) {
@@ -407,7 +411,8 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   // sx ring (a plain shared-memory flag; the epilogue polls it)
   volatile uint32_t* sx_tag = reinterpret_cast<volatile uint32_t*>(tmem_empty + kTmMaxAcc);
   uint64_t* drain = tmem_empty + kTmMaxAcc + kTmSxRing;  // MMA completion on the error path
-  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag
+  uint32_t* misc = reinterpret_cast<uint32_t*>(drain + 1);  // [0] tmem base, [1] last flag, [2..3] red_full
+  uint64_t* red_full = reinterpret_cast<uint64_t*>(misc + 2);  // push: the other ranks' partials have landed
   // streaming: [kTmSxRing][MT] ring indexed by j; resident: [slot][M]
   float* sx_ring = reinterpret_cast<float*>(misc + 4);
   float* ws_cache = sx_ring + kTmSxRing * MT;          // [min(J, kTmWsCache)]
@@ -473,6 +478,11 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
       mbar_init(&tmem_empty[lane], 4);   // 4 epilogue warps
     }
     if (lane == 0) mbar_init(drain, 1);
+    if (kCluster && lane == 0 && p.red_push && cluster_rank() == 0) {
+      // one phase: the bytes of csize - 1 partials
+      mbar_init(red_full, 1);
+      mbar_arrive_expect_tx(red_full, static_cast<uint32_t>((p.csize - 1) * p.M * 128 * 4));
+    }
     for (int r = lane; r < kTmSxRing; r += 32) sx_tag[r] = 0u;
     fence_mbar_init();
   } else if (warp == 1) {
@@ -484,6 +494,9 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // push: rank 0's barrier is initialised before any CTA of the cluster
+  // copies into it (the matching wait is at the reduction, long after)
+  if (kCluster && p.red_push) asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
   const uint32_t tmem_base = misc[0];
   bool ok = true;
 
@@ -1088,7 +1101,7 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
 #pragma unroll
           for (int m = 0; m < MT; ++m)
             if (m < p.M) store_out(m, n, __float2bfloat16_rn(acc[m]));
-        } else if (p.csize > 1) {
+        } else if (kCluster) {
           // cluster split-K: the partial sums stay in this CTA's shared memory
           // (the A tiles are free: every MMA has completed) and are reduced
           // across the cluster at the end of the kernel
@@ -1158,7 +1171,43 @@ gemm_tm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant
     }
   }
 
-  if (p.csize > 1) {
+  if (kCluster && p.red_push) {
+    // Cluster split-K reduction by push: every other CTA of the cluster copies
+    // its [M][128] partial sums (one bulk copy, shared memory to rank 0's
+    // shared memory) and is done; rank 0 waits for their bytes on red_full and
+    // adds the partials in rank order -- the same sums as the pull form below
+    // -- with one barrier wait instead of two cluster barriers.
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+    const int rank = static_cast<int>(cluster_rank());
+    const int nbc = static_cast<int>(u0 / p.KB);
+    float* part = reinterpret_cast<float*>(a_tiles);
+    float* red = reinterpret_cast<float*>(smem + p.red_off);
+    const uint32_t pbytes = static_cast<uint32_t>(p.M * 128 * 4);
+    if (warp >= 6) {
+      if (rank != 0) {
+        fence_proxy_async_smem();   // this thread's partial stores before the copy reads them
+        named_bar_sync(2, 128);
+        if (tid == 192) {
+          asm volatile(
+              "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  dsmem_addr(red + (rank - 1) * p.M * 128, 0)),
+              "r"(smem_u32(part)), "r"(pbytes), "r"(dsmem_addr(red_full, 0))
+              : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // part stays until it is read
+        }
+      } else {
+        named_bar_sync(2, 128);     // this CTA's own partial: written by the other epilogue threads
+        mbar_wait(red_full, 0, kSiteTmFixup);
+        for (int e = tid - 192; e < p.M * 128; e += 128) {
+          float sum = 0.0f;
+          sum += part[e];
+          for (int q = 1; q < p.csize; ++q) sum += red[(q - 1) * p.M * 128 + e];
+          store_out(e >> 7, nbc * 128 + (e & 127), __float2bfloat16_rn(sum));
+        }
+      }
+    }
+  } else if (kCluster) {
     // Cluster split-K reduction.  The CTAs of a cluster are the csize K parts
     // of one row block; after the barrier, epilogue thread t of cluster rank r
     // reduces elements e = r*128 + t (+ 128*csize ...) of the [M][128] partial
@@ -1442,6 +1491,22 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   if (p.norm.norm && !pl.resident) return 8;
   // tagged input words are read by the resident prologue only
   if (p.gather.tagged && p.gather.wait_input && !pl.resident) return 8;
+  // cluster split-K by push when rank 0's receive area fits beside the
+  // same feed (the ring may lose a stage); otherwise the pull form
+  p.red_push = 0;
+  p.red_off = 0;
+  if (csize > 1) {
+    const int64_t red_bytes = static_cast<int64_t>(csize - 1) * p.M * 128 * 4;
+    TmPlan pp;
+    if (red_bytes <= kTmPushMaxBytes &&
+        tm_plan<MT, SW>(&pp, p.M, p.U, p.KB, grid, sm_count, max_smem, p.prequant ? 0 : resident_mode,
+                        norm_bytes + red_bytes + 16, p.prequant != 0) &&
+        pp.resident == pl.resident) {
+      pl = pp;
+      p.red_push = 1;
+      p.red_off = static_cast<uint32_t>((pl.bar_off + TmCfg<MT, SW>::kTailBytes + norm_bytes + 15) / 16 * 16);
+    }
+  }
   p.stages = pl.stages;
   p.npw = pl.npw;
   p.resident = pl.resident;
@@ -1460,11 +1525,11 @@ int launch_tm_pass(const CUtensorMap& tw, const CUtensorMap& tx, TmParams p, int
   if (p.gather.world > 0 && p.gather.tagged) {
     // tagged words: calls of at most 16 tokens, the 16-token tile only
     if constexpr (MT == 16)
-      return go(gemm_tm_kernel<16, SW, true>);
+      return csize > 1 ? go(gemm_tm_kernel<16, SW, true, true>) : go(gemm_tm_kernel<16, SW, true, false>);
     else
       return 8;
   }
-  return go(gemm_tm_kernel<MT, SW, false>);
+  return csize > 1 ? go(gemm_tm_kernel<MT, SW, false, true>) : go(gemm_tm_kernel<MT, SW, false, false>);
 }
 
 // How many clusters of `csize` CTAs with `smem` bytes each can be resident at
@@ -1479,7 +1544,7 @@ int tm_max_clusters(int csize, size_t smem, int max_smem) {
   std::lock_guard<std::mutex> lock(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  auto fn = gemm_tm_kernel<MT, SW>;
+  auto fn = gemm_tm_kernel<MT, SW, false, true>;
   int n = 0;
   if (ensure_max_smem(reinterpret_cast<const void*>(fn), max_smem) == cudaSuccess &&
       (csize <= kTmMaxPortableCluster || ensure_nonportable_clusters(reinterpret_cast<const void*>(fn)) == cudaSuccess)) {
