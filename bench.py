@@ -16,15 +16,22 @@ sharded across the ranks, so the total work is fixed (strong scaling):
 down row-parallel, the row-parallel kernels storing their partial outputs
 into every rank's slabs over NVLink and the next column-parallel kernel
 adding them in its add + RMSNorm prologue (two exchanges per layer);
---tp-mode gather (default) shards every linear by output rows and its kernel stores
-its slice into every rank's output; --tp-mode nccl shards the same way and
-all-gathers with NCCL after each linear.
+--tp-mode tagged (default) shards every linear by output rows, its kernel
+storing its slice into every rank's output as tagged words (bf16 pairs with
+the call's sequence number) and each linear reading the previous one's output
+-- qkv -> o -> gate_up -> down -> the next layer's qkv -- by polling the words
+it reads; --tp-mode gather does the same with a flag raised after each
+kernel's stores, every linear reading its own input; --tp-mode nccl shards
+the same way and all-gathers with NCCL after each linear.
 
 value     algorithmic bytes per step / device time per step (CUDA graph of one
           step, CUDA events, max over ranks), in GB/s (whole job).
-e2e       the same metric through the public API (fp8gq.fused_gemv_quant,
-          eager) with the step's activations copied in from pinned host
-          memory and the outputs copied back, inside the timed region.
+e2e       the same metric through the public API (prepared launches of the
+          fp8gq calls, each half of the step captured once into a CUDA graph
+          and replayed, as a serving loop replays its decode step) with the
+          step's inputs copied in from pinned host memory and its outputs
+          copied back every step, inside the timed region (two copies of the
+          buffers, so a step's copies overlap its neighbours' compute).
 roofline  the dominant kernel (gate_up; at M = 1 the tile kernel): algorithmic
           bytes per launch / average launch duration (CUDA graph of 36 launches
           on distinct weights), against MEASURED_PEAKS.json's hbm_gbs.
@@ -61,7 +68,7 @@ WORKLOAD = ("qwen3-8b-fp8 decode linear stack, M=1: 36 layers x {qkv 4096->6144,
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
 # from the ncu captures summarised in profiles/ (single-GPU gate_up case)
 NCU_TRAFFIC_BYTES = {"gemv_row_kernel<false>": 100_719_872 + 3_674_368,
-                     "gemm_tm_kernel<16,false>": 100_812_032 + 3_818_752}
+                     "gemm_tm_kernel<16,false>": 100_812_032 + 3_818_752}   # keyed by ROUTED_KERNEL
 
 # M == 1 routing of fp8gq_fused_gemv_quant / fp8gq_fused_swiglu_q_gemm: the row
 # kernel for weights of at most 20 MiB (and K <= 49152), the tile kernel above.
@@ -95,16 +102,16 @@ def parse():
                     help="1 (default): declare the weights static (fp8gq.set_static_weights) -- no work "
                          "queued before a linear writes its weights, as in any decode step -- letting each "
                          "kernel fetch its first weight tiles before the previous one finishes; 0: do not")
-    ap.add_argument("--tp-mode", choices=["paired", "gather", "tagged", "nccl"], default="gather",
+    ap.add_argument("--tp-mode", choices=["paired", "gather", "tagged", "nccl"], default="tagged",
                     help="N > 1: paired -- qkv and gate_up column-parallel, o and down "
                          "row-parallel; each row-parallel kernel stores its partial into every rank's "
                          "slab over NVLink and the next column-parallel kernel adds the slabs in its "
-                         "add + RMSNorm prologue (two exchanges per layer); gather (default) -- every "
+                         "add + RMSNorm prologue (two exchanges per layer); gather -- every "
                          "linear N-sharded, the kernels store their output slices into every rank's buffer "
-                         "and raise a flag; tagged -- the same stores as tagged words, each linear reading "
-                         "the previous one's output (qkv -> o -> gate_up -> down -> next qkv) and polling "
-                         "the words it reads, no flags; nccl -- every linear N-sharded, an NCCL all-gather "
-                         "after each")
+                         "and raise a flag; tagged (default) -- the same stores as tagged words, each linear "
+                         "reading the previous one's output (qkv -> o -> gate_up -> down -> next qkv) and "
+                         "polling the words it reads, no flags; nccl -- every linear N-sharded, an NCCL "
+                         "all-gather after each")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
                          "<shape>[:row|:tm][:M=<m>] with shape in qkv,o,gate_up,down,swiglu_down, "
