@@ -102,7 +102,7 @@ def parse():
                     help="1 (default): declare the weights static (fp8gq.set_static_weights) -- no work "
                          "queued before a linear writes its weights, as in any decode step -- letting each "
                          "kernel fetch its first weight tiles before the previous one finishes; 0: do not")
-    ap.add_argument("--tp-mode", choices=["paired", "gather", "tagged", "nccl"], default="tagged",
+    ap.add_argument("--tp-mode", choices=["paired", "gather", "tagged", "chain", "nccl"], default="tagged",
                     help="N > 1: paired -- qkv and gate_up column-parallel, o and down "
                          "row-parallel; each row-parallel kernel stores its partial into every rank's "
                          "slab over NVLink and the next column-parallel kernel adds the slabs in its "
@@ -110,7 +110,8 @@ def parse():
                          "linear N-sharded, the kernels store their output slices into every rank's buffer "
                          "and raise a flag; tagged (default) -- the same stores as tagged words, each linear "
                          "reading the previous one's output (qkv -> o -> gate_up -> down -> next qkv) and "
-                         "polling the words it reads, no flags; nccl -- every linear N-sharded, an NCCL "
+                         "polling the words it reads, no flags; chain -- the tagged step's 144 linears in "
+                         "one persistent launch (fp8gq.ChainRunner); nccl -- every linear N-sharded, an NCCL "
                          "all-gather after each")
     ap.add_argument("--profile-case", default=None,
                     help="launch one kernel case --warmup + --steps times and exit (for ncu): "
@@ -517,7 +518,10 @@ def run_ours(args):
             dist.barrier()
 
     paired = world > 1 and args.tp_mode == "paired"
-    tagged = world > 1 and args.tp_mode == "tagged"
+    # chain: the tagged words of the tagged mode, the step's 144 linears in
+    # one persistent launch (fp8gq.ChainRunner) instead of one launch each
+    chain = world > 1 and args.tp_mode == "chain"
+    tagged = world > 1 and args.tp_mode in ("tagged", "chain")
     # ---- operands: each rank owns rows [r*N/world, (r+1)*N/world) of every
     # linear (gather / nccl modes), or, paired, rows of qkv and gate_up and
     # columns [r*K/world, (r+1)*K/world) of o and down
@@ -598,6 +602,16 @@ def run_ours(args):
         tagged_io = [chain_io(0), chain_io(1)]
         tdescs = [[pg.descriptor(o, rank * (SHAPES[k % len(SHAPES)][2] // world), w)
                    for k, (_, o, w) in enumerate(io)] for io in tagged_io]
+        if chain:
+            # link k reads linear k - 1's words, except layer 0's qkv (the step
+            # input); every link's input is the output of the one before it
+            runners = []
+            for io in tagged_io:
+                links = []
+                for k, (x, o, w) in enumerate(io):
+                    lin = layers[k // len(SHAPES)][k % len(SHAPES)]
+                    links.append(fp8gq.Link(x=x, w=lin[3], ws=lin[4], out=o, src=k - 1 if w else -1))
+                runners.append(fp8gq.ChainRunner(links, gather=pg))
     if paired:
         # Paired tensor parallelism, layer by layer:
         #   qkv      column-parallel, add + RMSNorm prologue over the sum of the
@@ -644,6 +658,10 @@ def run_ours(args):
         if paired:
             paired_step()
             return
+        if chain:
+            runners[0].run()
+            pg.decode(tagged_io[0][-1][1], dec2[0])
+            return
         if tagged:
             io = tagged_io[0]
             for k, (x, o, w) in enumerate(io):
@@ -669,6 +687,8 @@ def run_ours(args):
         runs it on the second copy of the inputs and outputs.  None for the
         NCCL mode (its all-gathers are not library launches)."""
         plans = []
+        if chain:
+            return None             # two launches per step: nothing to prepare
         if tagged:
             io = tagged_io[parity]
             for k, (x, o, w) in enumerate(io):
@@ -765,11 +785,18 @@ def run_ours(args):
         parity = layer_parity(layers[0], world, rank, dev)
     barrier()
 
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
+    # the timed step: a CUDA graph of it, or the chain's two launches issued
+    # as they are (a cooperative launch is not captured)
+    if chain:
+        graph = None
+        replay = step
+    else:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        replay = graph.replay
     for _ in range(3):
-        graph.replay()
+        replay()
     torch.cuda.synchronize()
     barrier()
 
@@ -788,7 +815,7 @@ def run_ours(args):
     e_a, e_b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_a.record()
     for _ in range(5):
-        graph.replay()
+        replay()
     e_b.record()
     torch.cuda.synchronize()
     est_ms = max(e_a.elapsed_time(e_b) / 5, 1e-3)
@@ -809,13 +836,13 @@ def run_ours(args):
         if nvc is not None:
             nvc.start()
         for _ in range(n_pre):
-            graph.replay()
+            replay()
         start.record()
         for _ in range(args.steps):
-            graph.replay()
+            replay()
         end.record()
         for _ in range(n_post):
-            graph.replay()
+            replay()
         torch.cuda.synchronize()
         nv_win = nvc.stop() if nvc is not None else None
         sampler.mark()
@@ -848,7 +875,7 @@ def run_ours(args):
                   "source": "NVML GPM NVLINK_TOTAL_TX/RX_PER_SEC over the loaded window, per rank",
                   "errors": [v[1] for v in allv if v[1]] or None}
     value = STEP_BYTES / (ms * 1e-3) / 1e9
-    launches = (LAYERS * len(SHAPES) + (1 if pg is not None else 0)) * args.steps
+    launches = (2 if chain else LAYERS * len(SHAPES) + (1 if pg is not None else 0)) * args.steps
 
     # ---- per-linear device time: graph of the 36 launches of one shape
     def graph_us(calls, reps=20):
@@ -1122,7 +1149,9 @@ def run_ours(args):
                       "runs and its outputs copied out while the step after runs, on two copy streams; each half "
                       "of the step captured once into a CUDA graph and replayed" if piped_ms is not None else
                       ", one run per step, copies before and after it (eager, no graph)"))
-                    if prepared is not None else "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
+                    if prepared is not None else
+                    "fp8gq.ChainRunner.run + PeerGather.decode per step (two launches), the step input in and the "
+                    "decoded result out" if chain else "fp8gq.fused_gemv_quant (eager) per linear + NCCL all-gather"),
            "eager_pipelined": ({"ms_per_step": round(piped_eager_ms, 4),
                                 "value": round(STEP_BYTES / (piped_eager_ms * 1e-3) / 1e9, 3),
                                 "path": "the same pipelined loop with the launch lists issued eagerly (no graph)"}
@@ -1134,6 +1163,7 @@ def run_ours(args):
            "eager_calls": {"ms_per_step": round(eager_ms, 4),
                            "value": round(STEP_BYTES / (eager_ms * 1e-3) / 1e9, 3),
                            "path": ("fp8gq.dist.PeerGather paired linears (eager)" if paired else
+                                    "fp8gq.ChainRunner.run + PeerGather.decode" if chain else
                                     "fp8gq.dist.PeerGather.linear (eager)" if pg is not None else
                                     "fp8gq.fused_gemv_quant (eager) per linear")}}
 
@@ -1161,6 +1191,10 @@ def run_ours(args):
                                             "o, down row-parallel; partials stored into every rank's slab by "
                                             "the kernels over NVLink and summed in the next linear's add + "
                                             "RMSNorm prologue") if paired else
+                                           (f"N-sharded x{world}, the step's 144 linears in one persistent "
+                                            "cooperative launch (fp8gq.ChainRunner), output slices stored into "
+                                            "every rank over NVLink as tagged words, each linear polling the "
+                                            "previous one's") if chain else
                                            (f"N-sharded x{world}, output slices stored into every rank by the "
                                             "kernels over NVLink as tagged words (each linear reading the "
                                             "previous one's output: qkv -> o -> gate_up -> down -> next qkv), "
@@ -1168,7 +1202,9 @@ def run_ours(args):
                                            (f"N-sharded x{world}, output slices stored into every rank by the "
                                             "kernels over NVLink") if pg is not None else
                                            f"N-sharded x{world} + NCCL all-gather per linear") if world > 1
-                           else "single GPU", "timing": "CUDA graph of one step, CUDA events",
+                           else "single GPU",
+                           "timing": ("the step's two launches (chain, decode) issued as they are, CUDA events"
+                                      if chain else "CUDA graph of one step, CUDA events"),
                            "static_weights": bool(args.static_weights)},
                 "us_per_call": {k: v["us_per_call"] for k, v in per.items()},
                 "per_linear": per, "per_linear_row_kernel": per_row, "per_linear_tile_kernel": per_tm, **extra,

@@ -147,7 +147,7 @@ typedef struct fp8gq_gather {
     uint32_t *seq;                           /* this rank: one uint32, zero-filled */
     int64_t ldo;                             /* row stride of the full outputs, elements */
     int col0;                                /* first column of this rank's slice */
-    int world;                               /* 2 .. FP8GQ_MAX_GATHER_RANKS */
+    int world;                               /* 1 .. FP8GQ_MAX_GATHER_RANKS (1: one GPU) */
     int rank;
     int wait_input;
     int local_out;                           /* 1: only wait; the output stays local
@@ -405,6 +405,60 @@ int fp8gq_stack_prepare(const fp8gq_stack_linear *lin, int n, int M, void *devic
  * run records a device error (fp8gq_device_error), its outputs are invalid
  * and the plan must be prepared again. */
 int fp8gq_stack_run(const fp8gq_stack_plan *plan, fp8gq_stream_t stream);
+
+/* Chain runner: a decode step's M == 1 linears, N-sharded across the ranks of
+ * a tagged gather (world 1 .. FP8GQ_MAX_GATHER_RANKS; world 1 is one GPU),
+ * in one persistent cooperative launch.  Linear i holds this rank's N rows
+ * (columns col0 .. col0 + N of its full output) and stores them as tagged
+ * words (see fp8gq_gather) into out[r] of every rank r.  Its input x is
+ * either the words of an earlier linear's output (src = that linear's index;
+ * x may point at any 16-byte aligned column of that output row, e.g. its
+ * first K columns) or, with src = -1, a bf16 row written before the launch.
+ * A linear polls the words it reads until they carry linear src's sequence
+ * number, so the list runs with no barrier or flag between linears, and the
+ * weight stream of later linears continues while a CTA waits for an input.
+ * The weights are static (fetched without waiting for earlier work).  The
+ * math and its order are the row kernel's (fp8gq_fused_gemv_quant_gather).
+ * Limits: M = 1, K <= 12288 (of gate and of up with swiglu), K and N
+ * multiples of 128.  After the launch this rank's sequence number has moved
+ * past the list (n numbers); fp8gq_gather_decode of the last linear's output
+ * reads it.  No counterpart in the reference (single-GPU, one launch per
+ * linear). */
+typedef struct fp8gq_chain_linear {
+    const void *x;                           /* src >= 0: words; src < 0: bf16 [K] (or [2K]) */
+    const void *w;   int64_t ldw;            /* e4m3 [N, ldw], this rank's rows */
+    const float *ws; int64_t ldws;           /* fp32 [N/128, ldws] */
+    int N, K;
+    int src;                                 /* the linear whose output x reads, or -1 */
+    int swiglu;                              /* 1: x is [gate | up], 2K columns */
+    int col0;                                /* this rank's first column in the full output */
+    int reserved;                            /* 0 */
+    void *out[FP8GQ_MAX_GATHER_RANKS];       /* rank r's output words of this linear */
+} fp8gq_chain_linear;
+
+/* Host-side record of a prepared chain (filled by fp8gq_chain_prepare). */
+typedef struct fp8gq_chain_plan {
+    void *device;                            /* the caller's device memory holding the list */
+    size_t bytes;
+    int n, device_id, grid, stages, world, rank;
+    size_t smem;
+    uint32_t *flags[FP8GQ_MAX_GATHER_RANKS];
+    uint32_t *counter, *seq;
+    int64_t reserved[4];
+} fp8gq_chain_plan;
+
+/* Device bytes a chain of n linears needs (its table). */
+size_t fp8gq_chain_plan_bytes(int n);
+
+/* Checks the list, copies it into device_mem (fp8gq_chain_plan_bytes(n),
+ * 256-byte aligned; a synchronous copy) and fills `plan`.  `gather` gives the
+ * tagged gather's flags, counter, seq, world and rank (its out, ldo, col0 and
+ * wait_input are not used). */
+int fp8gq_chain_prepare(const fp8gq_chain_linear *lin, int n, const fp8gq_gather *gather,
+                        void *device_mem, size_t bytes, fp8gq_chain_plan *plan);
+
+/* Launches a prepared chain on `stream` (cooperative: every CTA resident). */
+int fp8gq_chain_run(const fp8gq_chain_plan *plan, fp8gq_stream_t stream);
 
 /* Prepared launches.  A decode loop calls the same linears on the same
  * buffers every step; most of a call's host time is spent on work that does

@@ -21,6 +21,7 @@
 #include "swiglu_writer.cuh"
 #include "add_rmsnorm.cuh"
 #include "stack.cuh"
+#include "chain.cuh"
 
 using namespace fp8gq;
 
@@ -276,7 +277,7 @@ __global__ void gather_wait_kernel(const GatherParams g) {
 
 int to_gather_params(const fp8gq_gather* gather, GatherParams* g) {
   if (!gather || !gather->counter || !gather->seq) return FP8GQ_ERR_NULL_POINTER;
-  if (gather->world < 2 || gather->world > FP8GQ_MAX_GATHER_RANKS || gather->rank < 0 ||
+  if (gather->world < 1 || gather->world > FP8GQ_MAX_GATHER_RANKS || gather->rank < 0 ||
       gather->rank >= gather->world || gather->col0 < 0 || gather->ldo < 1)
     return FP8GQ_ERR_SHAPE;
   *g = GatherParams{};
@@ -948,6 +949,134 @@ int fp8gq_stack_run(const fp8gq_stack_plan* plan, fp8gq_stream_t stream) {
   if (e != cudaSuccess) return cuda_fail(e, "stack_kernel launch");
   e = cudaGetLastError();
   return e == cudaSuccess ? FP8GQ_OK : cuda_fail(e, "stack_kernel launch");
+}
+
+// ------------------------------------------------------------ chain runner --
+
+size_t fp8gq_chain_plan_bytes(int n) {
+  if (n < 1) return 0;
+  return (static_cast<size_t>(n) * sizeof(ChainLin) + 255) / 256 * 256;
+}
+
+int fp8gq_chain_prepare(const fp8gq_chain_linear* lin, int n, const fp8gq_gather* gather, void* device_mem,
+                        size_t bytes, fp8gq_chain_plan* plan) {
+  if (!lin || !gather || !device_mem || !plan) return FP8GQ_ERR_NULL_POINTER;
+  if (n < 1) return FP8GQ_ERR_SHAPE;
+  if (bytes < fp8gq_chain_plan_bytes(n)) return FP8GQ_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(device_mem) & 255u) return FP8GQ_ERR_ALIGNMENT;
+  if (!gather->counter || !gather->seq) return FP8GQ_ERR_NULL_POINTER;
+  const int world = gather->world;
+  if (world < 1 || world > FP8GQ_MAX_GATHER_RANKS || gather->rank < 0 || gather->rank >= world)
+    return FP8GQ_ERR_SHAPE;
+  for (int q = 0; q < world; ++q) {
+    if (!gather->flags[q]) return FP8GQ_ERR_NULL_POINTER;
+    if (reinterpret_cast<uintptr_t>(gather->flags[q]) & 3u) return FP8GQ_ERR_ALIGNMENT;
+  }
+  DeviceInfo di;
+  int dev = 0;
+  int st = device_info(&di, &dev);
+  if (st != FP8GQ_OK) return st;
+  std::vector<ChainLin> table(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) {
+    const fp8gq_chain_linear& a = lin[i];
+    ChainLin& c = table[static_cast<size_t>(i)];
+    if (!a.x || !a.w || !a.ws) return FP8GQ_ERR_NULL_POINTER;
+    if (a.N <= 0 || a.K <= 0 || a.N % kGroup || a.K % kGroup || a.K > kChainMaxK) return FP8GQ_ERR_SHAPE;
+    if (a.src < -1 || a.src >= i || a.reserved != 0) return FP8GQ_ERR_SHAPE;
+    if (a.ldw < a.K || a.ldws < a.K / kGroup) return FP8GQ_ERR_STRIDE;
+    if (!aligned16(a.w) || (a.ldw % 16) || !aligned16(a.x) || (reinterpret_cast<uintptr_t>(a.ws) & 3u) ||
+        a.col0 < 0 || (a.col0 % 2))
+      return FP8GQ_ERR_ALIGNMENT;
+    for (int r = 0; r < world; ++r) {
+      if (!a.out[r]) return FP8GQ_ERR_NULL_POINTER;
+      if (!aligned16(a.out[r])) return FP8GQ_ERR_ALIGNMENT;
+    }
+    c.x = a.x;
+    c.w = static_cast<const uint8_t*>(a.w);
+    c.ws = a.ws;
+    c.ldw = a.ldw;
+    c.ldws = a.ldws;
+    c.N = a.N;
+    c.K = a.K;
+    c.src = a.src;
+    c.swiglu = a.swiglu ? 1 : 0;
+    c.col0 = a.col0;
+    // rows per stage: the most (4, 2 or 1) whose stage is at most 16 KB, as
+    // the row kernel; with one row per stage the CTAs take rows in pairs (a
+    // tagged word holds two columns)
+    c.R = (4 * a.K <= kChainSlotBytes) ? 4 : (2 * a.K <= kChainSlotBytes) ? 2 : 1;
+    c.unit_stages = c.R == 1 ? 2 : 1;
+    c.units = c.R == 1 ? a.N / 2 : a.N / c.R;
+    for (int r = 0; r < kMaxGatherRanks; ++r) c.out[r] = r < world ? static_cast<uint64_t*>(a.out[r]) : nullptr;
+  }
+  cudaError_t e = cudaMemcpy(device_mem, table.data(), table.size() * sizeof(ChainLin), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "chain table copy");
+  const int stages = kChainRingBytes / kChainSlotBytes;
+  const size_t smem = static_cast<size_t>(stages) * kChainSlotBytes + 2 * stages * sizeof(uint64_t) +
+                      2 * (kChainThreads / 32) * kRowWindow * sizeof(float);
+  if (smem > static_cast<size_t>(di.max_smem_optin)) return FP8GQ_ERR_UNSUPPORTED;
+  e = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return cuda_fail(e, "chain_kernel shared memory attribute");
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kChainThreads + 32, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "chain_kernel occupancy");
+  if (per_sm < 1) return FP8GQ_ERR_UNSUPPORTED;
+  if (per_sm > 2) per_sm = 2;
+  *plan = fp8gq_chain_plan{};
+  plan->device = device_mem;
+  plan->bytes = bytes;
+  plan->n = n;
+  plan->device_id = dev;
+  plan->grid = per_sm * di.sm_count;
+  plan->stages = stages;
+  plan->world = world;
+  plan->rank = gather->rank;
+  plan->smem = smem;
+  for (int q = 0; q < world; ++q) plan->flags[q] = gather->flags[q];
+  plan->counter = gather->counter;
+  plan->seq = gather->seq;
+  return FP8GQ_OK;
+}
+
+int fp8gq_chain_run(const fp8gq_chain_plan* plan, fp8gq_stream_t stream) {
+  if (!plan || !plan->device || !plan->counter || !plan->seq) return FP8GQ_ERR_NULL_POINTER;
+  DeviceInfo di;
+  int dev = 0;
+  int st = device_info(&di, &dev);
+  if (st != FP8GQ_OK) return st;
+  if (dev != plan->device_id) return FP8GQ_ERR_DEVICE;
+  if (plan->n < 1 || plan->world < 1 || plan->world > FP8GQ_MAX_GATHER_RANKS || plan->grid < 1 ||
+      plan->stages != kChainRingBytes / kChainSlotBytes || plan->smem > static_cast<size_t>(di.max_smem_optin) ||
+      plan->grid > 2 * di.sm_count)
+    return FP8GQ_ERR_UNSUPPORTED;
+  ChainParams p;
+  p.lin = static_cast<const ChainLin*>(plan->device);
+  p.n = plan->n;
+  p.stages = plan->stages;
+  for (int q = 0; q < kMaxGatherRanks; ++q) p.flags[q] = q < plan->world ? plan->flags[q] : nullptr;
+  p.counter = plan->counter;
+  p.seq = plan->seq;
+  p.world = plan->world;
+  p.rank = plan->rank;
+  cudaError_t e = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(plan->smem));
+  if (e != cudaSuccess) return cuda_fail(e, "chain_kernel shared memory attribute");
+  // every CTA must be resident at once (they wait for one another's words):
+  // a cooperative grid, which the runtime refuses rather than run partly
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kChainThreads + 32);
+  cfg.dynamicSmemBytes = plan->smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, chain_kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "chain_kernel launch");
+  e = cudaGetLastError();
+  return e == cudaSuccess ? FP8GQ_OK : cuda_fail(e, "chain_kernel launch");
 }
 
 }  // extern "C"

@@ -24,6 +24,7 @@ from .ops import (GROUP, TM, ShapeError, add_rmsnorm, fused_add_rmsnorm_gemv_qua
 from .prepared import (LaunchList, Plan, prepare_fused_add_rmsnorm_gemv_quant, prepare_fused_gemv_quant,  # noqa: F401
                        prepare_fused_swiglu_q_gemm)
 from .stack import Linear, StackRunner  # noqa: F401
+from .chain import ChainRunner, Link  # noqa: F401
 
 __all__ = ["Fp8gqError", "ShapeError", "GROUP", "TM", "fused_gemv_quant", "fused_swiglu_q_gemm",
            "fused_swiglu", "fused_swiglu_quant", "add_rmsnorm", "fused_add_rmsnorm_gemv_quant",

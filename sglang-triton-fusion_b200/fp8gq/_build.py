@@ -14,7 +14,7 @@ SRC_DIR = PKG_DIR.parent / "csrc"
 REPO_DIR = PKG_DIR.parent.parent
 LIB_PATH = PKG_DIR / "libfp8gq.so"
 SOURCES = ["fp8gq_api.cu"]
-HEADERS = ["fp8gq_device.cuh", "gemv_row.cuh", "gemm_tm.cuh", "quant_only.cuh", "swiglu_writer.cuh",
+HEADERS = ["fp8gq_device.cuh", "gemv_row.cuh", "gemm_tm.cuh", "quant_only.cuh", "swiglu_writer.cuh", "chain.cuh",
            "add_rmsnorm.cuh", "stack.cuh"]
 
 NVCC_FLAGS = [

@@ -45,6 +45,23 @@ class Gather(ctypes.Structure):
                 ("tagged", ctypes.c_int)]
 
 
+class ChainLinear(ctypes.Structure):
+    """struct fp8gq_chain_linear (include/fp8gq.h)."""
+    _fields_ = [("x", ctypes.c_void_p), ("w", ctypes.c_void_p), ("ldw", ctypes.c_int64),
+                ("ws", ctypes.c_void_p), ("ldws", ctypes.c_int64), ("N", ctypes.c_int), ("K", ctypes.c_int),
+                ("src", ctypes.c_int), ("swiglu", ctypes.c_int), ("col0", ctypes.c_int), ("reserved", ctypes.c_int),
+                ("out", ctypes.c_void_p * MAX_GATHER_RANKS)]
+
+
+class ChainPlan(ctypes.Structure):
+    """struct fp8gq_chain_plan (include/fp8gq.h)."""
+    _fields_ = [("device", ctypes.c_void_p), ("bytes", ctypes.c_size_t),
+                ("n", ctypes.c_int), ("device_id", ctypes.c_int), ("grid", ctypes.c_int), ("stages", ctypes.c_int),
+                ("world", ctypes.c_int), ("rank", ctypes.c_int), ("smem", ctypes.c_size_t),
+                ("flags", ctypes.c_void_p * MAX_GATHER_RANKS), ("counter", ctypes.c_void_p),
+                ("seq", ctypes.c_void_p), ("reserved", ctypes.c_int64 * 4)]
+
+
 class LaunchPlan(ctypes.Structure):
     """struct fp8gq_launch_plan (include/fp8gq.h): opaque, copyable bytes."""
     _fields_ = [("opaque", ctypes.c_uint64 * 512)]
@@ -109,6 +126,10 @@ SIGNATURES = {
     "fp8gq_stack_dependencies": (_I, [ctypes.POINTER(StackLinear), _I, _I, ctypes.POINTER(_I)]),
     "fp8gq_stack_prepare": (_I, [ctypes.POINTER(StackLinear), _I, _I, _P, _SZ, ctypes.POINTER(StackPlan), _P]),
     "fp8gq_stack_run": (_I, [ctypes.POINTER(StackPlan), _P]),
+    "fp8gq_chain_plan_bytes": (_SZ, [_I]),
+    "fp8gq_chain_prepare": (_I, [ctypes.POINTER(ChainLinear), _I, ctypes.POINTER(Gather), _P, _SZ,
+                                 ctypes.POINTER(ChainPlan)]),
+    "fp8gq_chain_run": (_I, [ctypes.POINTER(ChainPlan), _P]),
     "fp8gq_gemv_quant_tm_noalloc": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P]),
     "fp8gq_prepare_fused_gemv_quant": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I, _I, _I, _P, _P, _P, _SZ,
                                             ctypes.POINTER(LaunchPlan)]),

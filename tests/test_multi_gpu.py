@@ -17,6 +17,8 @@ their output slices into every rank's buffer over NVLink (fp8gq.dist.PeerGather)
 * Paired tensor parallelism: row-parallel partials stored into every rank's
   slab, summed by the next column-parallel linear's reduce + add + RMSNorm
   prologue; each stage against the oracle.
+* The M = 1 tagged chain as one persistent launch (fp8gq.ChainRunner): every
+  stage against the oracle and across ranks, reruns with a rank held back.
 * The same chains with tagged words (PeerGather(tagged=True)): each linear
   reads the previous one's tagged output directly, the last stage of each
   chain a SwiGLU over a gathered [gate | up] output; every stage decoded on
@@ -293,6 +295,82 @@ def _tagged_chain_worker(rank, world, port, result_q):
 def test_tagged_chain_matches_oracle(world):
     _skip_unless(world)
     _spawn(_tagged_chain_worker, world)
+
+
+def _chain_runner_worker(rank, world, port, result_q):
+    """The M = 1 tagged chain as one persistent launch (fp8gq.ChainRunner),
+    every stage in its own buffer so that each can be checked afterwards."""
+    dev = _setup(rank, world, port)
+    import torch.distributed as dist
+
+    import fp8gq
+    from fp8gq import dist as fdist
+    errs = []
+    try:
+        fp8gq.load()
+        for ci, (M, stages) in enumerate(TAGGED_CHAINS):
+            if M != 1:
+                continue
+            n = len(stages)
+            sizes = [N // 2 for _, N, _ in stages]
+            words = torch.zeros(sum(sizes) + 32, dtype=torch.int64, device=dev)
+            pg = fdist.PeerGather(words, tagged=True)
+            outs, off = [], 0
+            for sz in sizes:
+                outs.append(words[off:off + sz].view(1, sz))
+                off += sz
+            lins, links = [], []
+            x0 = _activation(1, stages[0][0], 191 + ci, dev)
+            for j, (K, N, sw) in enumerate(stages):
+                wq, ws = _weight(N, K, 7000 + 100 * ci + j, dev)
+                lins.append((wq, ws) + fdist.shard_rows(wq, ws, rank, world))
+                x = x0 if j == 0 else outs[j - 1][:, :(2 * K if sw else K) // 2]
+                links.append(fp8gq.Link(x=x, w=lins[j][2], ws=lins[j][3], out=outs[j], src=j - 1, swiglu=sw))
+            runner = fp8gq.ChainRunner(links, gather=pg)
+            runner.run()
+            final = runner.decode(outs[-1])
+            torch.cuda.synchronize()
+            dist.barrier()
+            snaps = [fdist.untag(o) for o in outs[:-1]] + [final]
+            for j in range(n):
+                _same_on_every_rank(errs, f"chain runner {ci} stage {j}", snaps[j])
+            if rank == 0:
+                for j, (K, N, sw) in enumerate(stages):
+                    x = x0 if j == 0 else snaps[j - 1][:, :2 * K if sw else K]
+                    _oracle_check(errs, f"chain runner {ci} stage {j} ({'swiglu ' if sw else ''}{K}->{N})",
+                                  snaps[j], x, lins[j][0], lins[j][1], swiglu=sw)
+            # twice more back to back, the last rank held back before each
+            dist.barrier()
+            for _ in range(2):
+                if rank == world - 1:
+                    torch.cuda._sleep(SKEW_CYCLES)
+                runner.run()
+            again = runner.decode(outs[-1])
+            torch.cuda.synchronize()
+            if not torch.equal(again, final):
+                errs.append(f"chain runner {ci}: rerun changed the final output in "
+                            f"{(again != final).sum().item()} elements")
+            for j in range(n):
+                tg = fdist.tags(outs[j])
+                if not bool((tg == 2 * n + j + 1).all()):
+                    errs.append(f"chain runner {ci} stage {j}: tags {sorted(set(tg.flatten().tolist()))[:4]}, "
+                                f"expected {2 * n + j + 1}")
+            if fp8gq.device_error() != 0:
+                errs.append(f"device error word {fp8gq.device_error():#x}")
+            dist.barrier()
+            pg.close()
+        result_q.put((rank, errs))
+    except Exception as e:
+        result_q.put((rank, errs + [f"exception: {e!r}"]))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_chain_runner_matches_oracle(world):
+    _skip_unless(world)
+    _spawn(_chain_runner_worker, world)
 
 
 def _paired_worker(rank, world, port, result_q):
