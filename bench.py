@@ -68,7 +68,7 @@ WORKLOAD = ("qwen3-8b-fp8 decode linear stack, M=1: 36 layers x {qkv 4096->6144,
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant kernel,
 # from the ncu captures summarised in profiles/ (single-GPU gate_up case)
 NCU_TRAFFIC_BYTES = {"gemv_row_kernel<false>": 100_719_872 + 3_674_368,
-                     "gemm_tm_kernel<16,false>": 100_812_032 + 3_818_752}   # keyed by ROUTED_KERNEL
+                     "gemm_tm_kernel<16,false>": 100_815_616 + 3_400_448}   # keyed by ROUTED_KERNEL
 
 # M == 1 routing of fp8gq_fused_gemv_quant / fp8gq_fused_swiglu_q_gemm: the row
 # kernel for weights of at most 20 MiB (and K <= 49152), the tile kernel above.
